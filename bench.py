@@ -1,0 +1,409 @@
+#!/usr/bin/env python
+"""RBF kernel matrix forward + backward on B200: the headline benchmark.
+
+Metric: RBF fwd+bwd ms, GFLOP/s and % roofline at N=M=4096, D=64, with
+1/2/4/8-GPU scaling.  One "step" = forward K = rbf(X, Y) + backward (dX, dY) from an upstream
+gradient G, fp32 in and out.  FLOP per step = 6*N*M*D; algorithmic HBM bytes per step =
+12*N*M + 12*(N+M)*D.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c1]
+
+N = 1 runs config c1 (N=M=4096, D=64).  Under torchrun (WORLD_SIZE = N > 1) the work is
+weak-scaled by rows: every rank owns 4096 rows of X (and of G, K), Y (4096 x 64) is replicated,
+and the partial dY is summed with one NCCL all-reduce per step ("scaling": "weak").
+``value`` = whole-job GFLOP/s = (6 * N_global * M * D) / (max over ranks of the device time of
+one step).  Inputs are resident in HBM when timing starts; L2 is flushed (256 MiB write) before
+every timed step, outside the events.
+
+``--impl reference`` times the reference's own CPU implementation of the path (its broadcast
+``reference.py`` forward + torch autograd, restated in oracle/reference_port.py) on the host
+cores, on a bounded sample of rows per step, and prints the same JSON line with
+"impl": "reference".  Under torchrun only rank 0 runs it.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "nl2cuda-kernel-agent_b200")
+for _p in (PKG, ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "RBF fwd+bwd ms, GFLOP/s and % roofline at N=M=4096 D=64; 1/2/4/8 GPU scaling"
+UNIT = "GFLOP/s"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--config", default="c1")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="target CPU seconds of the cpu_baseline sample")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+                "source": "fallback"}
+
+
+def traffic_table():
+    """dram__bytes_read.sum + dram__bytes_write.sum per launch, from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu_id), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def nvsmi_id(device):
+    import torch
+    try:
+        return "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+    except Exception:
+        return device.index if device.index is not None else 0
+
+
+def workload(cfg_name, world):
+    from cases.rbf import config
+    c = dict(config.CONFIGS[cfg_name])
+    c["rows_per_rank"] = c["N"]
+    c["N_global"] = c["N"] * world
+    return c
+
+
+def run_reference(args, world, rank):
+    """The reference's CPU implementation (oracle/reference_port.py) on this host's cores."""
+    if rank != 0:
+        return
+    import torch
+    from oracle import reference_port
+    c = workload(args.config, world)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    N, M, D, g = c["N_global"], c["M"], c["D"], c["gamma"]
+    # One step = a bounded sample of rows of X against all of Y, sized to ~1 s of CPU work.
+    probe_s, probe_rows = reference_port.time_sample(N, M, D, g, 32, threads)
+    rows = int(max(8, min(N, 32 * max(1.0, 1.0 / max(probe_s, 1e-3)))))
+    gen = torch.Generator().manual_seed(0)
+    X = torch.randn(rows, D, generator=gen)
+    Y = torch.randn(M, D, generator=gen)
+    G = torch.randn(rows, M, generator=gen)
+    for _ in range(args.warmup):
+        reference_port.forward_backward(X, Y, G, g)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        reference_port.forward_backward(X, Y, G, g)
+        times.append(time.perf_counter() - t0)
+    per_row = statistics.mean(times) / rows
+    ms_step = per_row * N * 1e3  # extrapolated to the full workload (linear in rows)
+    gflops = 6.0 * rows * M * D / statistics.mean(times) / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gflops, 3), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.config}: RBF fwd+bwd N={N} M={M} D={D} gamma={g:.6g}",
+                   "N": N, "M": M, "D": D, "sample_rows_per_step": rows,
+                   "extrapolation": "ms_per_step scales the sample linearly to all N rows"},
+        "cpu_baseline": {"value": round(gflops, 3), "unit": UNIT, "cores": threads,
+                         "kind": "port",
+                         "sample": f"{rows} rows of X x all {M} rows of Y, fwd+bwd, per step"},
+        "e2e": {"value": round(gflops, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(c, seconds):
+    import torch
+    from oracle import reference_port
+    threads = os.cpu_count() or 1
+    N, M, D, g = c["N_global"], c["M"], c["D"], c["gamma"]
+    probe_s, _ = reference_port.time_sample(N, M, D, g, 16, threads)
+    rows = int(max(16, min(N, 16 * seconds / max(probe_s, 1e-3) / 2)))
+    sec, done = reference_port.time_sample(N, M, D, g, rows, threads)
+    torch.set_num_threads(threads)
+    return {"value": round(6.0 * done * M * D / sec / 1e9, 3), "unit": UNIT, "cores": threads,
+            "kind": "port",
+            "sample": f"{done} of {N} rows of X x all {M} rows of Y, fwd+bwd "
+                      f"({sec:.1f} s on {threads} threads)"}
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from cases.rbf import native, op, shard
+    from cases.rbf.reference import draw
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    c = workload(args.config, world)
+    n, M, D, g = c["rows_per_rank"], c["M"], c["D"], c["gamma"]
+    Ng = c["N_global"]
+
+    # Inputs: this rank's rows of X (and of G), Y replicated; resident in HBM.
+    X_all, Y = draw(1234, torch.float32, dev, n * world, M, D, c["ydist"], c["xscale"])
+    X = X_all[rank * n:(rank + 1) * n].contiguous()
+    del X_all
+    G = torch.randn(n, M, dtype=torch.float32, device=dev,
+                    generator=torch.Generator(device=dev).manual_seed(777 + rank))
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    compute = shard.NativeShardCompute()
+
+    def step():
+        return shard.forward_backward_shard(X, Y, G, g, compute=compute)
+
+    for _ in range(max(args.warmup, 0)):
+        step()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(nvsmi_id(dev))
+    sampler.start()
+    launches0 = native.launch_count()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    evs = []
+    for _ in range(args.steps):
+        flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        step()
+        b.record(stream)
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    launches = native.launch_count() - launches0
+    clocks = sampler.stop()
+    step_ms = [a.elapsed_time(b) for a, b in evs]
+    ms_local = statistics.mean(step_ms)
+    ms = shard.max_over_ranks(ms_local, device=dev)
+
+    # Dominant-kernel roofline: forward and backward timed alone on the launching stream.
+    def time_alone(fn, reps):
+        out = []
+        for _ in range(reps):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            out.append((a, b))
+        torch.cuda.synchronize()
+        return statistics.mean(a.elapsed_time(b) for a, b in out)
+
+    K, ws = native.forward_with_workspace(X, Y, g)
+    reps = max(args.steps, 5)
+    ms_fwd = time_alone(lambda: native.forward_with_workspace(X, Y, g), reps)
+    ms_bwd = time_alone(lambda: native.rbf_backward(X, Y, G, K, g, workspace=ws), reps)
+    pk = peaks()
+    fwd_bytes = 4 * n * M + 4 * (n + M) * D
+    bwd_bytes = 8 * n * M + 8 * (n + M) * D
+    bwd_flop = 4 * n * M * D
+    if ms_bwd >= ms_fwd:
+        kname, kms, kbytes = "rbf backward (prepared)", ms_bwd, bwd_bytes
+    else:
+        kname, kms, kbytes = "rbf forward (split + kernel)", ms_fwd, fwd_bytes
+    achieved = kbytes / (kms * 1e-3) / 1e9
+    tr = traffic_table().get(f"{kname}|{args.config}")
+    roofline = {"kernel": kname, "bound": "hbm", "achieved": round(achieved, 1),
+                "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                "traffic": tr, "peak_source": pk["source"],
+                "algorithmic_bytes_per_launch": kbytes, "ms_per_launch": round(kms, 5)}
+
+    # Whole-step roofline (BASELINE's % roofline): max(FLOP / P_tf32, bytes / HBM).
+    flop = 6.0 * Ng * M * D
+    p_tf32 = pk["bf16_tflops"] / 2.0 * 1e12
+    t_tc = 6.0 * n * M * D / p_tf32
+    t_hbm = (12.0 * n * M + 12.0 * (n + M) * D) / (pk["hbm_gbs"] * 1e9)
+    t_roof = max(t_tc, t_hbm)
+    gflops = flop / (ms * 1e-3) / 1e9
+
+    # End to end through the public API with host buffers.
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(X, Y, G, g, world, dev, args, shard, op)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(c, args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(gflops, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded X, Y, G with the config's distributions)",
+            "config": {"workload": f"{args.config}: RBF fwd+bwd fp32, {n} rows of X per rank "
+                                   f"(N={Ng} total), M={M}, D={D}, gamma={g:.6g}",
+                       "N": Ng, "M": M, "D": D, "rows_per_rank": n,
+                       "l2": "flushed before every timed step (256 MiB write, outside events)",
+                       "parallelism": f"row-shard x{world}" + (", dY all-reduce (NCCL)"
+                                                              if world > 1 else "")},
+            "ms_fwd": round(ms_fwd, 5), "ms_bwd": round(ms_bwd, 5),
+            "pct_roofline_step": round(100.0 * t_roof / (ms * 1e-3), 2),
+            "roofline_step_us": round(t_roof * 1e6, 2),
+            "roofline": roofline,
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(X, Y, G, g, world, dev, args, shard, op):
+    """Same metric through the public API, host buffers in and out: per step the H2D copy of
+    X (this rank's rows), Y and G from pinned memory, forward + backward, and the D2H copy of
+    K, dX and dY into pinned memory, all inside the events."""
+    import torch
+    Xh = X.cpu().pin_memory()
+    Yh = Y.cpu().pin_memory()
+    Gh = G.cpu().pin_memory()
+    n, D = X.shape
+    M = Y.shape[0]
+    Kh = torch.empty(n, M, dtype=torch.float32).pin_memory()
+    dXh = torch.empty(n, D, dtype=torch.float32).pin_memory()
+    dYh = torch.empty(M, D, dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+
+    def one():
+        Xd = Xh.to(dev, non_blocking=True)
+        Yd = Yh.to(dev, non_blocking=True)
+        Gd = Gh.to(dev, non_blocking=True)
+        if world == 1:
+            Xd.requires_grad_(True)
+            Yd.requires_grad_(True)
+            K = op.candidate({"X": Xd, "Y": Yd}, {"gamma": g})
+            K.backward(Gd)
+            dX, dY = Xd.grad, Yd.grad
+        else:
+            K, dX, dY = shard.forward_backward_shard(Xd, Yd, Gd, g)
+        Kh.copy_(K.detach(), non_blocking=True)
+        dXh.copy_(dX, non_blocking=True)
+        dYh.copy_(dY, non_blocking=True)
+
+    for _ in range(max(2, args.warmup)):
+        one()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(max(3, min(args.steps, 10))):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        one()
+        b.record(stream)
+        b.synchronize()
+        times.append(a.elapsed_time(b))
+    ms = shard.max_over_ranks(statistics.mean(times), device=dev)
+    flop = 6.0 * n * world * M * D
+    return {"value": round(flop / (ms * 1e-3) / 1e9, 2), "unit": UNIT, "ms_per_step": round(ms, 4),
+            "h2d_bytes_per_step": 4 * (n * D + M * D + n * M),
+            "d2h_bytes_per_step": 4 * (n * M + n * D + M * D),
+            "api": "cases.rbf.op.candidate + autograd" if world == 1
+                   else "cases.rbf.shard.forward_backward_shard"}
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,278 @@
+// rbf_api.cu -- the C ABI (include/rbf_sm100.h): argument validation, workspace carving and
+// kernel dispatch.  Every check that can fail on bad arguments runs on the host before any CUDA
+// call, so invalid calls return an rbf_status without touching the device.
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <atomic>
+#include <mutex>
+
+#include "rbf_common.cuh"
+#include "rbf_kernels.cuh"
+
+namespace rbf {
+
+static std::atomic<uint64_t> g_launches{0};
+void note_launches(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+namespace {
+
+thread_local char g_detail[512] = "";
+
+int set_detail(int status, const char* what, cudaError_t e = cudaSuccess) {
+  if (e != cudaSuccess) {
+    std::snprintf(g_detail, sizeof(g_detail), "%s: %s (%s)", what, cudaGetErrorName(e),
+                  cudaGetErrorString(e));
+  } else {
+    std::snprintf(g_detail, sizeof(g_detail), "%s", what);
+  }
+  return status;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Pointer rule: NULL is allowed only for an empty operand; non-NULL must be 16-byte aligned.
+int check_ptr(const void* p, int64_t elems, const char* name) {
+  if (elems == 0) return RBF_OK;
+  if (p == nullptr) {
+    char b[96];
+    std::snprintf(b, sizeof(b), "%s is NULL but has %lld elements", name, (long long)elems);
+    return set_detail(RBF_ERR_INVALID_ARGUMENT, b);
+  }
+  if (!aligned16(p)) {
+    char b[96];
+    std::snprintf(b, sizeof(b), "%s is not 16-byte aligned", name);
+    return set_detail(RBF_ERR_MISALIGNED, b);
+  }
+  return RBF_OK;
+}
+
+constexpr int64_t kMaxDim = int64_t(1) << 31;  // rows / cols of one call
+constexpr int64_t kMaxD = 4096;
+
+int check_shape(int64_t N, int64_t M, int64_t D, float gamma) {
+  if (N < 0 || M < 0 || D < 0) return set_detail(RBF_ERR_INVALID_ARGUMENT, "negative size");
+  if (N >= kMaxDim || M >= kMaxDim) return set_detail(RBF_ERR_UNSUPPORTED, "N or M >= 2^31");
+  if (D > kMaxD) return set_detail(RBF_ERR_UNSUPPORTED, "D > 4096");
+  if (!std::isfinite(gamma)) return set_detail(RBF_ERR_INVALID_ARGUMENT, "gamma is not finite");
+  return RBF_OK;
+}
+
+// The current device must be an sm_100 part (B200).  Cached per device ordinal.
+int check_device() {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_detail(RBF_ERR_NO_DEVICE, "cudaGetDevice", e);
+  static std::mutex mu;
+  static int cached[64];
+  static bool init = false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!init) {
+    for (int& c : cached) c = -1;
+    init = true;
+  }
+  if (dev >= 0 && dev < 64 && cached[dev] >= 0) return cached[dev];
+  int major = 0, minor = 0;
+  e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (e != cudaSuccess) return set_detail(RBF_ERR_CUDA, "cudaDeviceGetAttribute", e);
+  const int st = (major == 10 && minor == 0)
+                     ? RBF_OK
+                     : set_detail(RBF_ERR_NO_DEVICE, "current device is not sm_100 (B200)");
+  if (dev >= 0 && dev < 64) cached[dev] = st;
+  return st;
+}
+
+size_t backward_extra_bytes(int64_t N, int64_t M, int64_t D) {
+  (void)N; (void)M; (void)D;
+  return 0;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  return e == cudaSuccess ? RBF_OK : set_detail(RBF_ERR_CUDA, what, e);
+}
+
+int forward_impl(const float* X, const float* Y, float* K, int64_t N, int64_t M, int64_t D,
+                 float gamma, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  int st = check_shape(N, M, D, gamma);
+  if (st) return st;
+  if ((st = check_ptr(X, N * D, "X"))) return st;
+  if ((st = check_ptr(Y, M * D, "Y"))) return st;
+  if ((st = check_ptr(K, N * M, "K"))) return st;
+  const PrepLayout L = prep_layout(N, M, D);
+  if (ws == nullptr || ws_bytes < L.end) return set_detail(RBF_ERR_WORKSPACE, "forward workspace too small");
+  if (!aligned16(ws)) return set_detail(RBF_ERR_MISALIGNED, "workspace is not 16-byte aligned");
+  if ((st = check_device())) return st;
+  if ((st = cuda_status(launch_prep(X, Y, N, M, D, ws, stream), "split pass launch"))) return st;
+  return cuda_status(launch_forward_simt(X, Y, K, N, M, D, gamma, ws, stream), "forward launch");
+}
+
+int backward_impl(const float* X, const float* Y, const float* G, const float* K, float* dX,
+                  float* dY, int64_t N, int64_t M, int64_t D, float gamma, void* ws,
+                  size_t ws_bytes, cudaStream_t stream, bool prepared) {
+  int st = check_shape(N, M, D, gamma);
+  if (st) return st;
+  if ((st = check_ptr(X, N * D, "X"))) return st;
+  if ((st = check_ptr(Y, M * D, "Y"))) return st;
+  if ((st = check_ptr(G, N * M, "G"))) return st;
+  if ((st = check_ptr(K, N * M, "K"))) return st;
+  if ((st = check_ptr(dX, N * D, "dX"))) return st;
+  if ((st = check_ptr(dY, M * D, "dY"))) return st;
+  const PrepLayout L = prep_layout(N, M, D);
+  const size_t need = L.end + backward_extra_bytes(N, M, D);
+  if (ws == nullptr || ws_bytes < need) return set_detail(RBF_ERR_WORKSPACE, "backward workspace too small");
+  if (!aligned16(ws)) return set_detail(RBF_ERR_MISALIGNED, "workspace is not 16-byte aligned");
+  if ((st = check_device())) return st;
+  if (!prepared) {
+    if ((st = cuda_status(launch_prep(X, Y, N, M, D, ws, stream), "split pass launch"))) return st;
+  }
+  return cuda_status(launch_backward_simt(X, Y, G, K, dX, dY, N, M, D, gamma, stream),
+                     "backward launch");
+}
+
+}  // namespace
+}  // namespace rbf
+
+using namespace rbf;
+
+extern "C" {
+
+const char* rbf_sm100_strerror(int status) {
+  switch (status) {
+    case RBF_OK: return "success";
+    case RBF_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case RBF_ERR_MISALIGNED: return "pointer not 16-byte aligned";
+    case RBF_ERR_WORKSPACE: return "workspace missing or too small";
+    case RBF_ERR_UNSUPPORTED: return "unsupported shape";
+    case RBF_ERR_CUDA: return "CUDA error";
+    case RBF_ERR_NO_DEVICE: return "no sm_100 device is current";
+    case RBF_ERR_TIMEOUT: return "device-side wait timed out";
+    case RBF_ERR_TOO_LARGE: return "size exceeds the entry point's fixed capacity";
+    default: return "unknown rbf status";
+  }
+}
+
+const char* rbf_sm100_last_error_detail(void) { return g_detail; }
+
+int rbf_sm100_version(void) { return 100; }
+
+uint64_t rbf_sm100_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+size_t rbf_sm100_forward_workspace_bytes(int64_t N, int64_t M, int64_t D) {
+  if (N < 0 || M < 0 || D < 0) return 0;
+  return prep_layout(N, M, D).end;
+}
+
+size_t rbf_sm100_backward_workspace_bytes(int64_t N, int64_t M, int64_t D) {
+  if (N < 0 || M < 0 || D < 0) return 0;
+  return prep_layout(N, M, D).end + backward_extra_bytes(N, M, D);
+}
+
+int rbf_sm100_forward(const float* X, const float* Y, float* K, int64_t N, int64_t M, int64_t D,
+                      float gamma, void* workspace, size_t workspace_bytes, rbf_stream_t stream) {
+  return forward_impl(X, Y, K, N, M, D, gamma, workspace, workspace_bytes,
+                      reinterpret_cast<cudaStream_t>(stream));
+}
+
+int rbf_sm100_backward(const float* X, const float* Y, const float* G, const float* K, float* dX,
+                       float* dY, int64_t N, int64_t M, int64_t D, float gamma, void* workspace,
+                       size_t workspace_bytes, rbf_stream_t stream) {
+  return backward_impl(X, Y, G, K, dX, dY, N, M, D, gamma, workspace, workspace_bytes,
+                       reinterpret_cast<cudaStream_t>(stream), false);
+}
+
+int rbf_sm100_backward_prepared(const float* X, const float* Y, const float* G, const float* K,
+                                float* dX, float* dY, int64_t N, int64_t M, int64_t D,
+                                float gamma, void* workspace, size_t workspace_bytes,
+                                rbf_stream_t stream) {
+  return backward_impl(X, Y, G, K, dX, dY, N, M, D, gamma, workspace, workspace_bytes,
+                       reinterpret_cast<cudaStream_t>(stream), true);
+}
+
+int rbf_sm100_backward_shard(const float* X_local, const float* Y, const float* G_local,
+                             const float* K_local, float* dX_local, float* dY_partial,
+                             int64_t N_local, int64_t M, int64_t D, float gamma, void* workspace,
+                             size_t workspace_bytes, rbf_stream_t stream) {
+  return backward_impl(X_local, Y, G_local, K_local, dX_local, dY_partial, N_local, M, D, gamma,
+                       workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), false);
+}
+
+int rbf_sm100_read_status(void* workspace, rbf_stream_t stream, int* device_status) {
+  if (workspace == nullptr || device_status == nullptr)
+    return set_detail(RBF_ERR_INVALID_ARGUMENT, "NULL workspace or output");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int st = cuda_status(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+  if (st) return st;
+  int v = 0;
+  const PrepLayout L = prep_layout(0, 0, 0);
+  if ((st = cuda_status(cudaMemcpy(&v, ws_at<int>(workspace, L.status), sizeof(int),
+                                   cudaMemcpyDeviceToHost), "status copy")))
+    return st;
+  if ((st = cuda_status(cudaMemsetAsync(ws_at<int>(workspace, L.status), 0, sizeof(int), s),
+                        "status reset")))
+    return st;
+  *device_status = v;
+  return cuda_status(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+}
+
+// ---- legacy host-pointer ABI (reference cases/rbf/delivery/rbf_kernels.cu:168-220) --------
+
+static void legacy_check(int st, const char* what) {
+  if (st != RBF_OK) {
+    std::fprintf(stderr, "rbf: %s failed: %s (%s)\n", what, rbf_sm100_strerror(st), g_detail);
+    std::abort();
+  }
+}
+
+static void legacy_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) legacy_check(set_detail(RBF_ERR_CUDA, what, e), what);
+}
+
+void rbf_forward_cuda(const float* hX, const float* hY, float* hK, int N, int M, int D,
+                      float gamma) {
+  const size_t sx = sizeof(float) * (size_t)N * D, sy = sizeof(float) * (size_t)M * D,
+               sk = sizeof(float) * (size_t)N * M;
+  const size_t sw = rbf_sm100_forward_workspace_bytes(N, M, D);
+  float *dX = nullptr, *dY = nullptr, *dK = nullptr;
+  void* ws = nullptr;
+  legacy_cuda(cudaMalloc(&dX, sx ? sx : 16), "cudaMalloc");
+  legacy_cuda(cudaMalloc(&dY, sy ? sy : 16), "cudaMalloc");
+  legacy_cuda(cudaMalloc(&dK, sk ? sk : 16), "cudaMalloc");
+  legacy_cuda(cudaMalloc(&ws, sw), "cudaMalloc");
+  legacy_cuda(cudaMemcpy(dX, hX, sx, cudaMemcpyHostToDevice), "cudaMemcpy H2D");
+  legacy_cuda(cudaMemcpy(dY, hY, sy, cudaMemcpyHostToDevice), "cudaMemcpy H2D");
+  legacy_check(rbf_sm100_forward(dX, dY, dK, N, M, D, gamma, ws, sw, nullptr), "rbf_sm100_forward");
+  legacy_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  legacy_cuda(cudaMemcpy(hK, dK, sk, cudaMemcpyDeviceToHost), "cudaMemcpy D2H");
+  cudaFree(dX); cudaFree(dY); cudaFree(dK); cudaFree(ws);
+}
+
+void rbf_backward_cuda(const float* hX, const float* hY, const float* hG, const float* hK,
+                       float* hdX, float* hdY, int N, int M, int D, float gamma) {
+  const size_t sx = sizeof(float) * (size_t)N * D, sy = sizeof(float) * (size_t)M * D,
+               snm = sizeof(float) * (size_t)N * M;
+  const size_t sw = rbf_sm100_backward_workspace_bytes(N, M, D);
+  float *dX = nullptr, *dY = nullptr, *dG = nullptr, *dK = nullptr, *ddX = nullptr, *ddY = nullptr;
+  void* ws = nullptr;
+  legacy_cuda(cudaMalloc(&dX, sx ? sx : 16), "cudaMalloc");
+  legacy_cuda(cudaMalloc(&dY, sy ? sy : 16), "cudaMalloc");
+  legacy_cuda(cudaMalloc(&dG, snm ? snm : 16), "cudaMalloc");
+  legacy_cuda(cudaMalloc(&dK, snm ? snm : 16), "cudaMalloc");
+  legacy_cuda(cudaMalloc(&ddX, sx ? sx : 16), "cudaMalloc");
+  legacy_cuda(cudaMalloc(&ddY, sy ? sy : 16), "cudaMalloc");
+  legacy_cuda(cudaMalloc(&ws, sw), "cudaMalloc");
+  legacy_cuda(cudaMemcpy(dX, hX, sx, cudaMemcpyHostToDevice), "cudaMemcpy H2D");
+  legacy_cuda(cudaMemcpy(dY, hY, sy, cudaMemcpyHostToDevice), "cudaMemcpy H2D");
+  legacy_cuda(cudaMemcpy(dG, hG, snm, cudaMemcpyHostToDevice), "cudaMemcpy H2D");
+  legacy_cuda(cudaMemcpy(dK, hK, snm, cudaMemcpyHostToDevice), "cudaMemcpy H2D");
+  legacy_check(rbf_sm100_backward(dX, dY, dG, dK, ddX, ddY, N, M, D, gamma, ws, sw, nullptr),
+               "rbf_sm100_backward");
+  legacy_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  legacy_cuda(cudaMemcpy(hdX, ddX, sx, cudaMemcpyDeviceToHost), "cudaMemcpy D2H");
+  legacy_cuda(cudaMemcpy(hdY, ddY, sy, cudaMemcpyDeviceToHost), "cudaMemcpy D2H");
+  cudaFree(dX); cudaFree(dY); cudaFree(dG); cudaFree(dK); cudaFree(ddX); cudaFree(ddY);
+  cudaFree(ws);
+}
+
+}  // extern "C"

@@ -1,0 +1,122 @@
+"""Parity of the sm_100a path (through the C ABI) with the reference's outputs and the oracle."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from golden_util import load, names
+from gpu_util import TOL, assert_gate, run_path, to_dev
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("name", names())
+def test_golden_fixture(name, cuda_device):
+    z = load(name)
+    g = float(z["gamma"])
+    K, dX, dY = run_path(z["X"], z["Y"], z["G"], g)
+    assert_gate(f"{name} K", K, z["K"])
+    assert_gate(f"{name} dX", dX, z["dX"])
+    assert_gate(f"{name} dY", dY, z["dY"])
+
+
+SHAPES = [
+    (1, 1, 1, 0.5), (7, 129, 3, 0.3), (128, 128, 64, 1 / 64), (129, 257, 64, 1 / 64),
+    (300, 200, 100, 0.01), (257, 130, 32, 0.5 / 32), (64, 1000, 128, 1 / 128),
+    (1000, 333, 256, 1 / 256), (33, 65, 8, 0.2), (5, 3, 2048, 1 / 2048),
+]
+
+
+@pytest.mark.parametrize("N,M,D,gamma", SHAPES)
+def test_random_shapes_vs_oracle(N, M, D, gamma, cuda_device):
+    r = np.random.default_rng(N * 1000 + M + D)
+    X = r.standard_normal((N, D)).astype(np.float32)
+    Y = r.standard_normal((M, D)).astype(np.float32)
+    G = r.standard_normal((N, M)).astype(np.float32)
+    K, dX, dY = run_path(X, Y, G, gamma)
+    Kr = oracle.forward(X, Y, gamma)
+    dXr, dYr = oracle.backward(X, Y, G, gamma)
+    assert_gate("K", K, Kr)
+    assert_gate("dX", dX, dXr)
+    assert_gate("dY", dY, dYr)
+
+
+def test_prepared_and_shard_entries_agree(cuda_device):
+    from cases.rbf import native
+    r = np.random.default_rng(5)
+    X, Y = r.standard_normal((300, 64)), r.standard_normal((200, 64))
+    G = r.standard_normal((300, 200))
+    Xd, Yd, Gd = to_dev(X, Y, G)
+    K, ws = native.forward_with_workspace(Xd, Yd, 0.02)
+    a = native.rbf_backward(Xd, Yd, Gd, K, 0.02, workspace=ws)
+    b = native.rbf_backward(Xd, Yd, Gd, K, 0.02)
+    c = native.rbf_backward(Xd, Yd, Gd, K, 0.02, entry="rbf_sm100_backward_shard")
+    for u, v, w in zip(a, b, c):
+        assert torch.equal(u, v) and torch.equal(u, w)
+
+
+def test_forward_is_deterministic(cuda_device):
+    from cases.rbf import native
+    Xd, Yd = to_dev(*np.random.default_rng(9).standard_normal((2, 500, 64)))
+    K1 = native.rbf_forward(Xd, Yd, 1 / 64)
+    K2 = native.rbf_forward(Xd, Yd, 1 / 64)
+    assert torch.equal(K1, K2)
+
+
+def test_noncontiguous_and_misaligned_inputs(cuda_device):
+    from cases.rbf import native
+    r = np.random.default_rng(2)
+    big = to_dev(r.standard_normal((101, 7)))[0]
+    X = big[1:]          # 28-byte offset: not 16-byte aligned, copied by the binding
+    Y = to_dev(r.standard_normal((7, 50)))[0].t()   # non-contiguous
+    K = native.rbf_forward(X, Y, 0.3)
+    assert_gate("K", K.cpu().numpy(), oracle.forward(X.cpu().numpy(), Y.cpu().numpy(), 0.3))
+
+
+def test_errors_raise(cuda_device):
+    from cases.rbf import native
+    X = torch.randn(4, 3, device=cuda_device)
+    with pytest.raises(RuntimeError, match="share feature dim"):
+        native.rbf_forward(X, torch.randn(4, 5, device=cuda_device), 0.5)
+    with pytest.raises(RuntimeError, match="float32"):
+        native.rbf_forward(X.double(), X.double(), 0.5)
+    with pytest.raises(RuntimeError, match="not finite"):
+        native.rbf_forward(X, X, float("inf"))
+
+
+def test_legacy_host_pointer_abi(cuda_device):
+    from cases.rbf import native
+    L = native.lib()
+    r = np.random.default_rng(1234)
+    N, M, D, g = 128, 128, 64, 1 / 64  # the reference delivery self-test size
+    X = r.uniform(-1, 1, (N, D)).astype(np.float32)
+    Y = r.uniform(-1, 1, (M, D)).astype(np.float32)
+    G = r.uniform(-1, 1, (N, M)).astype(np.float32)
+    K = np.empty((N, M), np.float32)
+    dX = np.empty((N, D), np.float32)
+    dY = np.empty((M, D), np.float32)
+    fp = lambda a: a.ctypes.data_as(ctypes.c_void_p)  # noqa: E731
+    L.rbf_forward_cuda.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_float]
+    L.rbf_backward_cuda.argtypes = [ctypes.c_void_p] * 6 + [ctypes.c_int] * 3 + [ctypes.c_float]
+    L.rbf_forward_cuda(fp(X), fp(Y), fp(K), N, M, D, g)
+    L.rbf_backward_cuda(fp(X), fp(Y), fp(G), fp(K), fp(dX), fp(dY), N, M, D, g)
+    assert_gate("K", K, oracle.forward(X, Y, g))
+    dXr, dYr = oracle.backward(X, Y, G, g)
+    assert_gate("dX", dX, dXr)
+    assert_gate("dY", dY, dYr)
+
+
+def test_empty_sizes(cuda_device):
+    from cases.rbf import native
+    for (N, M, D) in [(0, 5, 3), (5, 0, 3), (4, 6, 0)]:
+        X = torch.randn(N, D, device=cuda_device)
+        Y = torch.randn(M, D, device=cuda_device)
+        G = torch.randn(N, M, device=cuda_device)
+        K, ws = native.forward_with_workspace(X, Y, 0.5)
+        dX, dY = native.rbf_backward(X, Y, G, K, 0.5, workspace=ws)
+        assert K.shape == (N, M) and dX.shape == (N, D) and dY.shape == (M, D)
+        if N and M:
+            assert torch.all(K == 1.0)  # D = 0: distance 0
+        assert torch.all(dX == 0) and torch.all(dY == 0)
