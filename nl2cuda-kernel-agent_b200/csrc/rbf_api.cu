@@ -16,6 +16,18 @@ namespace rbf {
 static std::atomic<uint64_t> g_launches{0};
 void note_launches(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
 
+WaitConfig wait_config_from_env() {
+  WaitConfig w;
+  w.timeout_ns = 2000ull * 1000000ull;
+  w.debug_skip_first_load = 0;
+  if (const char* s = std::getenv("RBF_WAIT_TIMEOUT_MS")) {
+    const long long ms = std::atoll(s);
+    if (ms > 0) w.timeout_ns = (unsigned long long)ms * 1000000ull;
+  }
+  if (const char* s = std::getenv("RBF_DEBUG_SKIP_FIRST_LOAD")) w.debug_skip_first_load = std::atoi(s) != 0;
+  return w;
+}
+
 namespace {
 
 thread_local char g_detail[512] = "";
@@ -105,7 +117,8 @@ int forward_impl(const float* X, const float* Y, float* K, int64_t N, int64_t M,
   if (!aligned16(ws)) return set_detail(RBF_ERR_MISALIGNED, "workspace is not 16-byte aligned");
   if ((st = check_device())) return st;
   if ((st = cuda_status(launch_prep(X, Y, N, M, D, ws, stream), "split pass launch"))) return st;
-  return cuda_status(launch_forward_simt(X, Y, K, N, M, D, gamma, ws, stream), "forward launch");
+  return cuda_status(launch_forward_tc(X, Y, K, N, M, D, gamma, ws, wait_config_from_env(), stream),
+                     "forward launch");
 }
 
 int backward_impl(const float* X, const float* Y, const float* G, const float* K, float* dX,

@@ -1,0 +1,360 @@
+// rbf_fwd_tc.cu -- the RBF forward on the sm_100a tensor cores.
+//
+//   K[i,j] = exp(-gamma * max(||x_i||^2 + ||y_j||^2 - 2 x_i.y_j, 0))
+//
+// x_i.y_j is a dense contraction over D; it runs on tcgen05 tensor cores in 3xTF32:
+//   x.y ~= xhi.yhi + xhi.ylo + xlo.yhi
+// where hi is the TF32-exact top of each fp32 value and lo the fp32 remainder (both written by
+// the split pass, rbf_prep.cu).  The dropped lo.lo term and the TF32 rounding of lo are below
+// 2^-20 relative, so the product has fp32-level accuracy.
+//
+// Kernel organisation (one persistent CTA per SM, 320 threads):
+//   warp 0    TMA producer: per stage one 32-feature slice of Xhi, Xlo (128 rows each) and of
+//             Yhi, Ylo (128 rows each), 128-byte swizzled, into a 3-deep ring (64 KiB/stage).
+//   warp 1    MMA issuer (one thread): 3 x tcgen05.mma.kind::tf32 (M=128, N=128, K=8) per 8
+//             features into one of two TMEM accumulators (2 x 128 columns), so the epilogue of
+//             tile t overlaps the MMAs of tile t+1.
+//   warps 2-9 epilogue: warp w reads TMEM lanes 32*(w%4).. (its row quadrant) and one half of
+//             the columns, adds the norms, clamps, exponentiates (MUFU ex2), stages 32x32 fp32
+//             blocks in swizzled shared memory and writes them with TMA stores (no multicast).
+// Every mbarrier wait is bounded (globaltimer); on expiry the kernel records RBF_ERR_TIMEOUT in
+// the workspace status word, waits (bounded) for its own copies in flight, frees TMEM and
+// returns.
+//
+// HBM roofline per launch: K write 4*N*M bytes + X/Y split reads; tensor work 3 * 2*N*M*Dp.
+#include <cuda.h>
+
+#include <algorithm>
+
+#include "rbf_common.cuh"
+#include "rbf_kernels.cuh"
+#include "rbf_ptx.cuh"
+
+namespace rbf {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int BK = 32;
+constexpr int STAGES = 3;
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 32 * (2 + EPI_WARPS);
+constexpr uint32_t TILE_BYTES = 128 * BK * 4;  // 16 KiB: 128 rows x 128 bytes
+constexpr uint32_t STAGE_BYTES = 4 * TILE_BYTES;
+constexpr uint32_t EPI_BYTES = 32 * 32 * 4;    // one 32x32 fp32 staging block per warp
+constexpr uint32_t TMEM_COLS = 2 * BN;
+constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + EPI_WARPS * EPI_BYTES + 256;
+static_assert(SMEM_BYTES <= 232448, "forward shared memory over the sm_100 limit");
+
+struct FwdArgs {
+  const float* xn;
+  const float* yn;
+  float* K;  // direct-store epilogue only
+  int64_t N, M;
+  int tiles_m, tiles_n, num_kc;
+  float scale;  // -gamma * log2(e)
+  int* status;
+  unsigned long long timeout_ns;
+  int debug_skip_first_load;
+};
+
+template <bool TMA_STORE>
+__global__ void __launch_bounds__(THREADS, 1)
+    rbf_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_xhi,
+                      const __grid_constant__ CUtensorMap tm_xlo,
+                      const __grid_constant__ CUtensorMap tm_yhi,
+                      const __grid_constant__ CUtensorMap tm_ylo,
+                      const __grid_constant__ CUtensorMap tm_k, const FwdArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* stage_mem = smem;
+  uint8_t* epi_mem = smem + STAGES * STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_mem + EPI_WARPS * EPI_BYTES);
+  uint64_t* full = bars;                  // [STAGES]  TMA -> MMA
+  uint64_t* empty = bars + STAGES;        // [STAGES]  MMA -> TMA
+  uint64_t* acc_full = bars + 2 * STAGES; // [2]       MMA -> epilogue
+  uint64_t* acc_empty = acc_full + 2;     // [2]       epilogue -> MMA
+  uint64_t* drain = acc_empty + 2;        // [1]       MMA teardown
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(&acc_full[b], 1);
+      ptx::mbar_init(&acc_empty[b], EPI_WARPS);
+    }
+    ptx::mbar_init(drain, 1);
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tensormap(&tm_xhi);
+    ptx::prefetch_tensormap(&tm_xlo);
+    ptx::prefetch_tensormap(&tm_yhi);
+    ptx::prefetch_tensormap(&tm_ylo);
+    if (TMA_STORE) ptx::prefetch_tensormap(&tm_k);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, TMEM_COLS);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int num_tiles = a.tiles_m * a.tiles_n;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int last_parity[STAGES];
+      for (int s = 0; s < STAGES; ++s) last_parity[s] = -1;
+      bool ok = true;
+      bool skipped = false;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int i0 = (t % a.tiles_m) * BM;
+        const int j0 = (t / a.tiles_m) * BN;
+        for (int kc = 0; kc < a.num_kc; ++kc) {
+          if (!ptx::mbar_wait_bounded(&empty[stage], phase ^ 1, a.status, a.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          if (a.debug_skip_first_load && !skipped && blockIdx.x == 0) {
+            skipped = true;  // test hook: this stage never fills, so its consumer times out
+          } else {
+            uint8_t* sm = stage_mem + stage * STAGE_BYTES;
+            ptx::mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+            ptx::tma_load_2d(sm, &tm_xhi, kc * BK, i0, &full[stage]);
+            ptx::tma_load_2d(sm + TILE_BYTES, &tm_xlo, kc * BK, i0, &full[stage]);
+            ptx::tma_load_2d(sm + 2 * TILE_BYTES, &tm_yhi, kc * BK, j0, &full[stage]);
+            ptx::tma_load_2d(sm + 3 * TILE_BYTES, &tm_ylo, kc * BK, j0, &full[stage]);
+            last_parity[stage] = (int)phase;
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Error path: let every load this thread issued land before the CTA exits.
+        for (int s = 0; s < STAGES; ++s)
+          if (last_parity[s] >= 0)
+            ptx::mbar_wait_bounded(&full[s], (uint32_t)last_parity[s], a.status, a.timeout_ns);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = ptx::idesc_tf32(BM, BN, 0, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (!ptx::mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1, a.status, a.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(acc * BN);
+        for (int kc = 0; kc < a.num_kc; ++kc) {
+          if (!ptx::mbar_wait_bounded(&full[stage], phase, a.status, a.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t base = ptx::smem_u32(stage_mem + stage * STAGE_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 8; ++k) {
+            const uint32_t off = (uint32_t)k * 32;  // 8 tf32 = 32 bytes along the swizzled row
+            const uint64_t ahi = ptx::smem_desc(base + off, 16, 1024, 2);
+            const uint64_t alo = ptx::smem_desc(base + TILE_BYTES + off, 16, 1024, 2);
+            const uint64_t bhi = ptx::smem_desc(base + 2 * TILE_BYTES + off, 16, 1024, 2);
+            const uint64_t blo = ptx::smem_desc(base + 3 * TILE_BYTES + off, 16, 1024, 2);
+            ptx::mma_tf32_ss(d, ahi, bhi, idesc, (kc | k) != 0);
+            ptx::mma_tf32_ss(d, ahi, blo, idesc, 1);
+            ptx::mma_tf32_ss(d, alo, bhi, idesc, 1);
+          }
+          ptx::mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        ptx::mma_commit(&acc_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+      // Teardown: every MMA issued so far must finish before TMEM is freed.
+      ptx::mma_commit(drain);
+      ptx::mbar_wait_bounded(drain, 0, a.status, a.timeout_ns);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;              // TMEM lane quadrant this warp may access
+    const int h = (warp - 2) >> 2;       // column half of the tile
+    uint8_t* buf = epi_mem + (warp - 2) * EPI_BYTES;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      const int64_t i0 = (int64_t)(t % a.tiles_m) * BM;
+      const int64_t j0 = (int64_t)(t / a.tiles_m) * BN;
+      if (!ptx::mbar_wait_bounded(&acc_full[acc], acc_phase, a.status, a.timeout_ns)) break;
+      ptx::tc_fence_after();
+      const int64_t i = i0 + q * 32 + lane;
+      const float xi = i < a.N ? __ldg(a.xn + i) : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        const int col0 = h * 64 + c * 32;
+        uint32_t v[32];
+        ptx::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + col0), v);
+        ptx::tmem_wait_ld();
+        if (c == 1) {
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&acc_empty[acc]);
+        }
+        const int64_t j = j0 + col0;
+        float yv[32];
+        if (j + 32 <= a.M) {
+          const float4* y4 = reinterpret_cast<const float4*>(a.yn + j);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float4 f = __ldg(y4 + e);
+            yv[4 * e] = f.x; yv[4 * e + 1] = f.y; yv[4 * e + 2] = f.z; yv[4 * e + 3] = f.w;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) yv[e] = (j + e < a.M) ? __ldg(a.yn + j + e) : 0.f;
+        }
+        float out[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float d2 = fmaxf(fmaf(-2.f, __uint_as_float(v[e]), xi + yv[e]), 0.f);
+          out[e] = exp2_approx(d2 * a.scale);
+        }
+        if (TMA_STORE) {
+          if (lane == 0) ptx::bulk_wait_read<0>();  // previous store has read the buffer
+          __syncwarp();
+          uint8_t* row = buf + lane * 128;
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4) {
+            *reinterpret_cast<float4*>(row + ((c4 ^ (lane & 7)) << 4)) =
+                make_float4(out[4 * c4], out[4 * c4 + 1], out[4 * c4 + 2], out[4 * c4 + 3]);
+          }
+          ptx::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            ptx::tma_store_2d(&tm_k, buf, (int32_t)j, (int32_t)(i0 + q * 32));
+            ptx::bulk_commit();
+          }
+        } else if (i < a.N) {
+          float* krow = a.K + i * a.M;
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (j + e < a.M) krow[j + e] = out[e];
+        }
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+    if (TMA_STORE && lane == 0) ptx::bulk_wait<0>();
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ----------------------------------------------------------------------- host side
+
+}  // namespace
+
+// 2-D fp32 tensor map: `rows` x `cols` row-major with row pitch `pitch_elems`, box
+// box_cols x box_rows, 128-byte swizzle, zero fill out of bounds.
+bool make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                  uint64_t pitch_elems, uint32_t box_cols, uint32_t box_rows) {
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {pitch_elems * sizeof(float)};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int device_sm_count() {
+  int dev = 0, n = kSmCount;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : kSmCount;
+}
+
+cudaError_t launch_forward_tc(const float* X, const float* Y, float* K, int64_t N, int64_t M,
+                              int64_t D, float gamma, void* ws, const WaitConfig& wc,
+                              cudaStream_t stream) {
+  (void)X; (void)Y;
+  if (N == 0 || M == 0) return cudaSuccess;
+  const PrepLayout L = prep_layout(N, M, D);
+  CUtensorMap txh, txl, tyh, tyl, tk;
+  if (!make_tmap_2d(&txh, ws_at<float>(ws, L.xhi), N, L.Dp, L.Dp, BK, 128) ||
+      !make_tmap_2d(&txl, ws_at<float>(ws, L.xlo), N, L.Dp, L.Dp, BK, 128) ||
+      !make_tmap_2d(&tyh, ws_at<float>(ws, L.yhi), M, L.Dp, L.Dp, BK, 128) ||
+      !make_tmap_2d(&tyl, ws_at<float>(ws, L.ylo), M, L.Dp, L.Dp, BK, 128))
+    return cudaErrorInvalidValue;
+  const bool tma_store = (M % 4) == 0;
+  if (tma_store) {
+    if (!make_tmap_2d(&tk, K, N, M, M, 32, 32)) return cudaErrorInvalidValue;
+  } else {
+    tk = txh;  // unused by the direct-store epilogue
+  }
+  FwdArgs a;
+  a.xn = ws_at<float>(ws, L.xn);
+  a.yn = ws_at<float>(ws, L.yn);
+  a.K = K;
+  a.N = N;
+  a.M = M;
+  a.tiles_m = (int)ceil_div(N, BM);
+  a.tiles_n = (int)ceil_div(M, BN);
+  a.num_kc = (int)(L.Dp / BK);
+  a.scale = (float)(-(double)gamma * 1.4426950408889634);
+  a.status = ws_at<int>(ws, L.status);
+  a.timeout_ns = wc.timeout_ns;
+  a.debug_skip_first_load = wc.debug_skip_first_load;
+  const int64_t tiles = (int64_t)a.tiles_m * a.tiles_n;
+  const int grid = (int)std::min<int64_t>(tiles, device_sm_count());
+  cudaError_t e;
+  if (tma_store) {
+    e = cudaFuncSetAttribute(rbf_fwd_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    rbf_fwd_tc_kernel<true><<<grid, THREADS, SMEM_BYTES, stream>>>(txh, txl, tyh, tyl, tk, a);
+  } else {
+    e = cudaFuncSetAttribute(rbf_fwd_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    rbf_fwd_tc_kernel<false><<<grid, THREADS, SMEM_BYTES, stream>>>(txh, txl, tyh, tyl, tk, a);
+  }
+  note_launches(1);
+  return cudaGetLastError();
+}
+
+}  // namespace rbf

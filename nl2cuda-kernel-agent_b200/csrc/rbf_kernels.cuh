@@ -6,6 +6,21 @@
 
 namespace rbf {
 
+// Bound of every device-side mbarrier wait, and the test hook that makes one wait run out.
+// Read from the environment at each call: RBF_WAIT_TIMEOUT_MS (default 2000) and
+// RBF_DEBUG_SKIP_FIRST_LOAD (default 0; 1 = CTA 0 of the tensor-core kernels never fills its
+// first pipeline stage, so the consumer's wait times out and the status word reports it).
+struct WaitConfig {
+  unsigned long long timeout_ns;
+  int debug_skip_first_load;
+};
+WaitConfig wait_config_from_env();
+
+// rbf_fwd_tc.cu: the tcgen05 3xTF32 forward (workspace must hold the split pass output).
+cudaError_t launch_forward_tc(const float* X, const float* Y, float* K, int64_t N, int64_t M,
+                              int64_t D, float gamma, void* ws, const WaitConfig& wc,
+                              cudaStream_t stream);
+
 // rbf_prep.cu: norms + TF32 hi/lo split of X and Y into the workspace.
 cudaError_t launch_prep(const float* X, const float* Y, int64_t N, int64_t M, int64_t D,
                         void* ws, cudaStream_t stream);

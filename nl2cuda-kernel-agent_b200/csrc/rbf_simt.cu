@@ -139,6 +139,7 @@ cudaError_t launch_forward_simt(const float* X, const float* Y, float* K, int64_
 cudaError_t launch_backward_simt(const float* X, const float* Y, const float* G, const float* K,
                                  float* dX, float* dY, int64_t N, int64_t M, int64_t D,
                                  float gamma, cudaStream_t stream) {
+  if (D == 0) return cudaSuccess;  // dX and dY are empty
   const float c = -2.f * gamma;
   const unsigned dblocks = (unsigned)ceil_div(D, 64);
   if (N > 0) {
