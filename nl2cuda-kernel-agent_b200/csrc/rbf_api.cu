@@ -140,6 +140,10 @@ int backward_impl(const float* X, const float* Y, const float* G, const float* K
   if (!prepared) {
     if ((st = cuda_status(launch_prep(X, Y, N, M, D, ws, stream), "split pass launch"))) return st;
   }
+  if (backward_tc_supported(N, M, D))
+    return cuda_status(launch_backward_tc(X, Y, G, K, dX, dY, N, M, D, gamma, ws,
+                                          wait_config_from_env(), stream),
+                       "backward launch");
   return cuda_status(launch_backward_simt(X, Y, G, K, dX, dY, N, M, D, gamma, stream),
                      "backward launch");
 }

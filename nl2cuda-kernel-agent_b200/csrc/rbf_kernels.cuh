@@ -1,6 +1,7 @@
 // rbf_kernels.cuh -- host-side launchers of the kernels in this directory (C++ linkage,
 // internal to the library; the public C ABI is include/rbf_sm100.h).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -24,6 +25,19 @@ cudaError_t launch_forward_tc(const float* X, const float* Y, float* K, int64_t 
 // rbf_prep.cu: norms + TF32 hi/lo split of X and Y into the workspace.
 cudaError_t launch_prep(const float* X, const float* Y, int64_t N, int64_t M, int64_t D,
                         void* ws, cudaStream_t stream);
+
+// rbf_fwd_tc.cu host helpers shared by the tensor-core kernels.
+bool make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                  uint64_t pitch_elems, uint32_t box_cols, uint32_t box_rows,
+                  int swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
+int device_sm_count();
+
+// rbf_bwd_tc.cu: the fused tcgen05 3xTF32 backward (zeroes dX, dY, then accumulates into
+// them).  Needs M % 4 == 0 (16-byte pitched rows of G and K for TMA).
+bool backward_tc_supported(int64_t N, int64_t M, int64_t D);
+cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, const float* K,
+                               float* dX, float* dY, int64_t N, int64_t M, int64_t D,
+                               float gamma, void* ws, const WaitConfig& wc, cudaStream_t stream);
 
 // rbf_simt.cu: fp32 CUDA-core kernels (bring-up path).
 cudaError_t launch_forward_simt(const float* X, const float* Y, float* K, int64_t N, int64_t M,

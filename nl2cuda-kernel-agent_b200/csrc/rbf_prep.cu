@@ -15,7 +15,9 @@ namespace rbf {
 __global__ void __launch_bounds__(256) prep_split_kernel(
     const float* __restrict__ X, const float* __restrict__ Y, int64_t N, int64_t M, int64_t D,
     int64_t Dp, float* __restrict__ xn, float* __restrict__ yn, float* __restrict__ xhi,
-    float* __restrict__ xlo, float* __restrict__ yhi, float* __restrict__ ylo) {
+    float* __restrict__ xlo, float* __restrict__ yhi, float* __restrict__ ylo,
+    int* __restrict__ status) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) *status = RBF_OK;  // fresh workspace: no error yet
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (warp >= N + M) return;
@@ -48,7 +50,7 @@ cudaError_t launch_prep(const float* X, const float* Y, int64_t N, int64_t M, in
   prep_split_kernel<<<(unsigned)blocks, 32 * warps_per_block, 0, stream>>>(
       X, Y, N, M, D, L.Dp, ws_at<float>(ws, L.xn), ws_at<float>(ws, L.yn),
       ws_at<float>(ws, L.xhi), ws_at<float>(ws, L.xlo), ws_at<float>(ws, L.yhi),
-      ws_at<float>(ws, L.ylo));
+      ws_at<float>(ws, L.ylo), ws_at<int>(ws, L.status));
   note_launches(1);
   return cudaGetLastError();
 }
