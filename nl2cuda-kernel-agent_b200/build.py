@@ -69,7 +69,7 @@ def build(verbose=False, ptxas_info=False, force=False, name="rbf_sm100", srcs=N
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
-    cmd = [NVCC, *ARCH_FLAGS, "-shared", "-o", lib + ".tmp", *objs, "-lcuda"]
+    cmd = [NVCC, *ARCH_FLAGS, "-shared", "-o", lib + ".tmp", *objs]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

@@ -291,13 +291,32 @@ __global__ void __launch_bounds__(THREADS, 1)
 // box_cols x box_rows, zero fill out of bounds.  `swizzle` is CU_TENSOR_MAP_SWIZZLE_128B for
 // K-major MMA operands and staging tiles, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B for MN-major
 // tf32 operands (the only shared-memory layout the tensor core accepts for those).
+// cuTensorMapEncodeTiled is reached through the runtime's driver entry-point table, so the
+// library loads (and its host-side checks run) on machines without a CUDA driver.
+using EncodeTiledFn = decltype(&cuTensorMapEncodeTiled);
+
+static EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
 bool make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
                   uint64_t pitch_elems, uint32_t box_cols, uint32_t box_rows, int swizzle) {
+  const EncodeTiledFn enc = encode_tiled();
+  if (enc == nullptr) return false;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {pitch_elems * sizeof(float)};
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = cuTensorMapEncodeTiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims,
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, (CUtensorMapSwizzle)swizzle,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
