@@ -120,6 +120,25 @@ RBF_API int rbf_sm100_backward_shard(const float* X_local, const float* Y, const
 RBF_API int rbf_sm100_read_status(void* workspace, rbf_stream_t stream, int* device_status);
 
 /* ---------------------------------------------------------------------------------------------
+ * Allocation-free forward.  No counterpart in the reference.  For callers that cannot allocate
+ * device memory (an application whose allocator owns the device heap, a runtime that forbids
+ * cudaMalloc on its hot path, a plugin interface with no way to pass a workspace): same result
+ * as rbf_sm100_forward, but the workspace is a fixed device array inside this library
+ * (rbf_sm100_forward_noalloc_capacity() bytes, 16 MiB, held on every GPU that loads the library
+ * until the process exits).  The caller still passes X, Y and K.  Calls whose workspace would
+ * exceed the capacity return RBF_ERR_TOO_LARGE (about (N+M)*(2*Dp+1)*4 bytes are needed,
+ * Dp = D rounded up to 32; e.g. N = M = 4096 at D = 64 fits).  Allocates nothing: no cudaMalloc,
+ * no cudaFree, no allocating library call.  The first call on each device looks up the
+ * array's device address with that device current (cudaGetSymbolAddress); make that first
+ * call before any stream capture.  All calls share the one array, so calls that overlap on the
+ * GPU (different streams, or other host threads) race and must be serialised by the caller.
+ * ------------------------------------------------------------------------------------------- */
+RBF_API size_t rbf_sm100_forward_noalloc_capacity(void);
+RBF_API int rbf_sm100_forward_noalloc(const float* X, const float* Y, float* K,
+                                      int64_t N, int64_t M, int64_t D, float gamma,
+                                      rbf_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
  * Legacy host-pointer ABI of the reference's standalone delivery
  * (reference cases/rbf/delivery/rbf_kernels.cu:168-220, delivery/README.md:37-41):
  * host pointers, blocking, device memory allocated and freed inside every call.  Like the

@@ -293,3 +293,72 @@ void rbf_backward_cuda(const float* hX, const float* hY, const float* hG, const 
 }
 
 }  // extern "C"
+
+// ---- allocation-free forward ------------------------------------------------------------
+//
+// Some callers cannot allocate device memory: a host runtime whose allocator owns the whole
+// device heap, an embedding that forbids cudaMalloc on its hot path, or a plugin with no
+// workspace argument to pass through.  rbf_sm100_forward_noalloc serves them with a workspace
+// that lives in this file-scope device array instead of a caller buffer.  Every GPU that loads
+// the library reserves these bytes until the process exits.
+namespace rbf {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch for the current device, looked up once per device.  In
+// host code the array's name is only a stand-in, never a device address, so the address must
+// come from cudaGetSymbolAddress with that device current.
+int noalloc_scratch(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_detail(RBF_ERR_NO_DEVICE, "cudaGetDevice", e);
+  static std::mutex mu;
+  static void* addr[64] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 0 || dev >= 64) return set_detail(RBF_ERR_NO_DEVICE, "device ordinal >= 64");
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return set_detail(RBF_ERR_CUDA, "cudaGetSymbolAddress(scratch)", e);
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return RBF_OK;
+}
+
+}  // namespace
+}  // namespace rbf
+
+extern "C" size_t rbf_sm100_forward_noalloc_capacity(void) { return rbf::kNoAllocScratchBytes; }
+
+extern "C" int rbf_sm100_forward_noalloc(const float* X, const float* Y, float* K, int64_t N,
+                                         int64_t M, int64_t D, float gamma,
+                                         rbf_stream_t stream) {
+  using namespace rbf;
+  int st = check_shape(N, M, D, gamma);
+  if (st) return st;
+  if ((st = check_ptr(X, N * D, "X"))) return st;
+  if ((st = check_ptr(Y, M * D, "Y"))) return st;
+  if ((st = check_ptr(K, N * M, "K"))) return st;
+  const PrepLayout L = prep_layout(N, M, D);
+  if (L.end > kNoAllocScratchBytes) {
+    char b[256];
+    std::snprintf(b, sizeof(b),
+                  "needs %zu bytes of scratch for N=%lld M=%lld D=%lld; the allocation-free "
+                  "forward holds %zu (use rbf_sm100_forward with a workspace)",
+                  L.end, (long long)N, (long long)M, (long long)D, kNoAllocScratchBytes);
+    return set_detail(RBF_ERR_TOO_LARGE, b);
+  }
+  if ((st = check_device())) return st;
+  void* ws = nullptr;
+  if ((st = noalloc_scratch(&ws))) return st;
+  // The split pass rewrites every scratch byte the forward reads (norms, hi/lo splits) and
+  // resets the status word, so nothing left by an earlier call leaks into this one.
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if ((st = cuda_status(launch_prep(X, Y, N, M, D, ws, s), "split pass launch"))) return st;
+  return cuda_status(launch_forward_tc(X, Y, K, N, M, D, gamma, ws, wait_config_from_env(), s),
+                     "forward launch");
+}
