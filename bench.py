@@ -251,9 +251,23 @@ def main():
         step()
     torch.cuda.synchronize()
 
+    # The timed step is replayed from a CUDA graph: the host work of the Python binding (tens of
+    # microseconds per call) stays out of the device timeline.  The graph holds every kernel and
+    # memset of one forward + backward (+ the NCCL all-reduce when N > 1).
+    def capture(fn):
+        gr = torch.cuda.CUDAGraph()
+        before = native.launch_count()
+        with torch.cuda.graph(gr):
+            fn()
+        return gr, native.launch_count() - before
+
+    step_graph, launches_per_step = capture(step)
+    for _ in range(max(args.warmup, 0)):
+        step_graph.replay()
+    torch.cuda.synchronize()
+
     sampler = ClockSampler(nvsmi_id(dev))
     sampler.start()
-    launches0 = native.launch_count()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -264,36 +278,40 @@ def main():
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        step()
+        step_graph.replay()
         b.record(stream)
         evs.append((a, b))
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    launches = native.launch_count() - launches0
+    launches = launches_per_step * args.steps
     clocks = sampler.stop()
     step_ms = [a.elapsed_time(b) for a, b in evs]
     ms_local = statistics.mean(step_ms)
     ms = shard.max_over_ranks(ms_local, device=dev)
 
-    # Dominant-kernel roofline: forward and backward timed alone on the launching stream.
-    def time_alone(fn, reps):
+    # Dominant-kernel roofline: the forward (split pass + kernel) and the backward kernel, each
+    # replayed alone from its own graph, timed with events on the launching stream.
+    def time_alone(gr, reps):
         out = []
         for _ in range(reps):
             flush.zero_()
             a = torch.cuda.Event(enable_timing=True)
             b = torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            fn()
+            gr.replay()
             b.record(stream)
             out.append((a, b))
         torch.cuda.synchronize()
         return statistics.mean(a.elapsed_time(b) for a, b in out)
 
     K, ws = native.forward_with_workspace(X, Y, g)
+    torch.cuda.synchronize()
+    fwd_graph, _ = capture(lambda: native.forward_with_workspace(X, Y, g))
+    bwd_graph, _ = capture(lambda: native.rbf_backward(X, Y, G, K, g, workspace=ws))
     reps = max(args.steps, 5)
-    ms_fwd = time_alone(lambda: native.forward_with_workspace(X, Y, g), reps)
-    ms_bwd = time_alone(lambda: native.rbf_backward(X, Y, G, K, g, workspace=ws), reps)
+    ms_fwd = time_alone(fwd_graph, reps)
+    ms_bwd = time_alone(bwd_graph, reps)
     pk = peaks()
     fwd_bytes = 4 * n * M + 4 * (n + M) * D
     bwd_bytes = 8 * n * M + 8 * (n + M) * D
