@@ -97,8 +97,7 @@ int check_device() {
 }
 
 size_t backward_extra_bytes(int64_t N, int64_t M, int64_t D) {
-  (void)N; (void)M; (void)D;
-  return 0;
+  return backward_scratch_bytes(N, M, D);
 }
 
 int cuda_status(cudaError_t e, const char* what) {

@@ -4,34 +4,42 @@
 //   dX[i,:] = c * ( rowsum_j(W)[i] * x_i - sum_j W[i,j] y_j )
 //   dY[j,:] = c * ( colsum_i(W)[j] * y_j - sum_i W[i,j] x_i )
 //
-// G and K are read from HBM exactly once, in tiles of 128 (i) x 128 (j) that arrive as four
-// strips of 32 rows (TMA, 128-byte swizzle).  W is formed on the CUDA cores in two mappings:
-//   C-warps (thread <-> column j): per strip, W^T[j, 32 rows] -> TF32 hi/lo -> TMEM lanes j,
-//     the A operand of the dY product  D_dY[j,d] += W^T[j,i] X[i,d]  (tcgen05.mma, A in TMEM,
-//     B = the strip's X rows in shared memory, MN-major).  colsum_j accumulates in a register.
-//   R-warps (thread <-> row i): W[i, 128 columns] -> hi/lo -> TMEM lanes i, the A operand of
-//     D_dX[i,d] += W[i,j] Y[j,d] (B = the CTA's resident Y tile).  rowsum_i in a register.
-// Both products are 3xTF32 (hi*hi + hi*lo + lo*hi), fp32 accumulation in TMEM.
-// MN-major tf32 operands must use the "128-byte swizzle, 32-byte atom" shared-memory layout
-// (descriptor layout type 1; 4-row K groups); the X and Y tensor maps load them that way
-// (CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B).
+// Tiles of 128 (i) x 128 (j).  G and K are read from HBM once, as four column strips per tile
+// (128 i x 32 j: one 32x128 TMA box each, 128-byte swizzle) through a 4-deep ring -- strip s of
+// every tile uses stage s, so one whole tile is in flight.  Both products are 3xTF32
+// (hi*hi + hi*lo + lo*hi, fp32 accumulation in TMEM) with A in TMEM:
+//   R-warps (thread <-> row i): per strip W[i, 32 j] -> TF32 hi/lo -> TMEM lanes i, the A
+//     operand of  D_dX[i,:] += W[i,j] Y[j,:]  (B = the strip's Y rows); rowsum_i.  Streamed:
+//     two W buffers, one dX MMA batch per strip.
+//   C-warp q (thread <-> column j of quadrant q): from strip q, W^T[j, all 128 i] -> TMEM lanes
+//     j, the A operand of  D_dY[j,:] += W^T[j,i] X[i,:]  (B = X rows, four 32-row chunks);
+//     colsum_j.  The W^T tile (256 columns) is resident for one tile; the dY batch runs once
+//     all four quadrants are written.
+// The B operands (X, Y rows, features contiguous) are MN-major and use the 128-byte-swizzle /
+// 32-byte-atom layout (descriptor layout type 1, TMA CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B): the
+// only shared-memory layout the tensor core accepts for MN-major tf32.
 //
 // Work split: tiles are ordered (feature slice, j-block, i-block) and every CTA takes a
-// contiguous range, so within a j-block segment the dY accumulator stays in TMEM across all its
-// i-blocks.  The dX accumulator covers one tile (128 columns) and is flushed after every tile;
-// flushes and segment ends add c*(sum * x - acc) into dX / dY with vector red.global.add (the
-// outputs are zeroed first), so no partial buffers exist.  Features are processed in slices of
-// DS (32 or 64) columns; D > 64 runs one slice per segment (G and K are re-read per slice).
+// contiguous range, so within a j-block "segment" the dY accumulator stays in TMEM across all
+// its i-blocks and is flushed at the segment end (red.add of c*(colsum*y - acc)).  The dX
+// accumulator is flushed once per tile: -c*acc is staged in shared memory and added into dX by
+// a TMA reduce-add, rowsum is added into a per-row vector, and a finalize pass adds
+// c*rowsum*x once per row.  The outputs are zeroed first; the fp32 summation order of dX / dY
+// varies between runs.  Features are processed in slices of DS (32 or 64); D > 64 runs one
+// slice per segment (G and K are re-read per slice).  D % 4 != 0 flushes dX with red.add too.
 //
-// TMEM (512 columns): [0,64) dY acc | [64,128) dX acc | [128,256) two W^T buffers (hi,lo x 32)
-//                     | [256,384) W hi (128 cols) | [384,512) W lo.
-// Shared memory: a 3-deep ring of strips (G 16 KiB + K 16 KiB + X hi/lo rows) and the resident
-// Y hi/lo tile of the current j-block.
-// Warps: 0 TMA producer, 1 MMA issuer, 2-5 C-warps, 6-9 R-warps (warp w owns TMEM lanes
-// 32*(w%4)..+31).  Every mbarrier wait is bounded; a timeout is recorded in the status word.
+// TMEM (512 columns): [0,64) dY acc | [64,128) dX acc | [128,256) two W buffers (hi 32 + lo
+// 32) | [256,384) W^T hi (128 columns of i) | [384,512) W^T lo.
+// Shared memory (DS = 64): strip ring 4 x 32 KiB, X ring 2 x 16 KiB, Y ring 2 x 16 KiB, dX
+// staging 4 x 8 KiB.
+// Warps: 0 TMA producer of strips + Y rows, 1 TMA producer of X rows, 2 dY MMA issuer, 3 dX MMA
+// issuer, 4-7 C-warps, 8-11 R-warps (warp w reaches TMEM lanes 32*(w%4)..+31).  Independent
+// pipelines sit in different warps: a lane blocked in mbarrier.try_wait holds back its whole
+// warp.  Every mbarrier wait is bounded; a timeout is recorded in the workspace status word.
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "rbf_common.cuh"
 #include "rbf_kernels.cuh"
@@ -41,22 +49,24 @@ namespace rbf {
 namespace {
 
 constexpr int BT = 128;        // tile edge (rows of i and columns of j)
-constexpr int SR = 32;         // strip rows
-constexpr int STAGES = 3;
-constexpr int THREADS = 320;
-constexpr uint32_t BOX = 32 * 32 * 4;  // one 32x32 fp32 TMA box, 4 KiB
-constexpr uint32_t COL_DY = 0, COL_DX = 64, COL_WT = 128, COL_W = 256;
-constexpr uint32_t MN_SBO = 512;       // 4 K-rows x 128 B: one K group of the 32B-atom layout
+constexpr int SR = 32;         // strip width
+constexpr int STAGES = 4;      // strip ring: one stage per strip of a tile
+constexpr int XSTAGES = 2;     // X-row ring
+constexpr int YSTAGES = 2;     // Y-row ring
+constexpr int THREADS = 384;
+constexpr uint32_t BOX = 32 * 32 * 4;       // 32x32 fp32, 4 KiB
+constexpr uint32_t STRIP = 128 * 32 * 4;    // one column strip of G (or K), 16 KiB
+constexpr uint32_t COL_DY = 0, COL_DX = 64, COL_W = 128, COL_WT = 256;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t MN_SBO = 512;       // one K group (4 rows x 128 B) of the 32B-atom layout
 constexpr uint32_t MN_LAYOUT = 1;      // descriptor layout type: 128B swizzle, 32B atom
 
 template <int DS>
 struct Cfg {
-  static constexpr uint32_t G_BYTES = 4 * BOX;                  // strip of G: 32 x 128
-  static constexpr uint32_t X_BYTES = (DS / 32) * BOX;          // strip of X (hi or lo)
-  static constexpr uint32_t STAGE_BYTES = 2 * G_BYTES + 2 * X_BYTES;
-  static constexpr uint32_t YBOX = 128 * 32 * 4;                // 128 j rows x 32 features
-  static constexpr uint32_t Y_BYTES = (DS / 32) * YBOX;         // Y tile (hi or lo)
-  static constexpr size_t SMEM = 1024 + STAGES * STAGE_BYTES + 2 * Y_BYTES + 512;
+  static constexpr uint32_t X_BYTES = (DS / 32) * BOX;   // 32 rows x DS features, hi or lo
+  static constexpr uint32_t STAGING = X_BYTES;           // one R-warp's dX flush: 32 x DS
+  static constexpr size_t SMEM = 1024 + STAGES * 2 * STRIP + XSTAGES * 2 * X_BYTES +
+                                 YSTAGES * 2 * X_BYTES + 4 * STAGING + 512;
 };
 static_assert(Cfg<64>::SMEM <= 232448, "backward shared memory over the sm_100 limit");
 
@@ -65,6 +75,7 @@ struct BwdArgs {
   const float* Y;
   float* dX;
   float* dY;
+  float* rowsum;  // [N] sum_j W[i,j], accumulated here when the dX flush goes through TMA
   int64_t N, M, D;
   int tiles_i, tiles_j, num_slices;
   int64_t total_tiles;
@@ -72,11 +83,32 @@ struct BwdArgs {
   int* status;
   unsigned long long timeout_ns;
   int debug_skip_first_load;
+  int tma_flush;  // dX partials are added by TMA reduce (needs D % 4 == 0)
+  int ablate;     // development builds only (RBF_TRACE): 1 skip dX reduce, 2 skip rowsum add
 };
 
 struct TileCoord {
   int slice, jb, ib;
 };
+
+#ifdef RBF_TRACE
+// Development timeline of CTA 0 (built only with -DRBF_TRACE): per role, events packed as
+// (code << 56 | globaltimer).  Read back with rbf_debug_trace().
+__device__ unsigned long long g_trace[8][1024];
+__device__ int g_trace_n[8];
+__device__ unsigned long long g_cta_span[1024][2];
+__device__ __forceinline__ void trace(int role, int code) {
+  if (blockIdx.x != 0) return;
+  const int n = g_trace_n[role];
+  if (n < 1024) {
+    g_trace[role][n] = ((unsigned long long)code << 56) | (ptx::globaltimer() & ((1ull << 56) - 1));
+    g_trace_n[role] = n + 1;
+  }
+}
+#define TRACE(role, code) trace(role, code)
+#else
+#define TRACE(role, code) ((void)0)
+#endif
 
 __device__ __forceinline__ TileCoord tile_of(int64_t t, const BwdArgs& a) {
   TileCoord c;
@@ -87,11 +119,13 @@ __device__ __forceinline__ TileCoord tile_of(int64_t t, const BwdArgs& a) {
   return c;
 }
 
+__device__ __forceinline__ bool same_segment(const TileCoord& p, const TileCoord& q) {
+  return p.slice == q.slice && p.jb == q.jb;
+}
+
 __device__ __forceinline__ bool segment_ends(int64_t t, int64_t t_end, const TileCoord& tc,
                                              const BwdArgs& a) {
-  if (t + 1 == t_end) return true;
-  const TileCoord n = tile_of(t + 1, a);
-  return n.slice != tc.slice || n.jb != tc.jb;
+  return t + 1 == t_end || !same_segment(tile_of(t + 1, a), tc);
 }
 
 __device__ __forceinline__ void red_add4(float* p, float a, float b, float c, float d) {
@@ -146,306 +180,376 @@ __global__ void __launch_bounds__(THREADS, 1)
                       const __grid_constant__ CUtensorMap tm_xhi,
                       const __grid_constant__ CUtensorMap tm_xlo,
                       const __grid_constant__ CUtensorMap tm_yhi,
-                      const __grid_constant__ CUtensorMap tm_ylo, const BwdArgs a) {
+                      const __grid_constant__ CUtensorMap tm_ylo,
+                      const __grid_constant__ CUtensorMap tm_dx, const BwdArgs a) {
   using C = Cfg<DS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* ring = smem;
-  uint8_t* ytile = smem + STAGES * C::STAGE_BYTES;  // [Y hi | Y lo]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ytile + 2 * C::Y_BYTES);
-  uint64_t* full = bars;                 // [STAGES] TMA -> consumers
-  uint64_t* empty = full + STAGES;       // [STAGES] consumers -> TMA
-  uint64_t* wt_full = empty + STAGES;    // [2]      C-warps -> MMA
-  uint64_t* wt_empty = wt_full + 2;      // [2]      MMA -> C-warps
-  uint64_t* w_full = wt_empty + 2;       // R-warps -> MMA
-  uint64_t* dx_full = w_full + 1;        // MMA -> R-warps
-  uint64_t* dx_empty = dx_full + 1;      // R-warps -> MMA
-  uint64_t* dy_full = dx_empty + 1;      // MMA -> C-warps
-  uint64_t* dy_empty = dy_full + 1;      // C-warps -> MMA
-  uint64_t* y_full = dy_empty + 1;       // TMA -> MMA
-  uint64_t* y_empty = y_full + 1;        // MMA -> TMA
-  uint64_t* drain = y_empty + 1;         // MMA teardown
-  uint64_t* r_full = drain + 1;          // [4] C-warps -> R-warp s: strip s of a tile landed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(r_full + 4);
+  uint8_t* ring = smem;                                 // [STAGES][G strip | K strip]
+  uint8_t* xring = ring + STAGES * 2 * STRIP;           // [XSTAGES][X hi | X lo]
+  uint8_t* yring = xring + XSTAGES * 2 * C::X_BYTES;    // [YSTAGES][Y hi | Y lo]
+  uint8_t* staging = yring + YSTAGES * 2 * C::X_BYTES;  // [4 R-warps][32 rows x DS]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(staging + 4 * C::STAGING);
+  uint64_t* full = bar;              // [4] strip landed            TMA -> R-warps, C-warp
+  uint64_t* empty = full + 4;        // [4] strip consumed          R-warps, C-warp -> TMA
+  uint64_t* xfull = empty + 4;       // [2] X rows landed           TMA -> dY issuer
+  uint64_t* xempty = xfull + 2;      // [2] X rows consumed         dY issuer -> TMA
+  uint64_t* yfull = xempty + 2;      // [2] Y rows landed           TMA -> dX issuer
+  uint64_t* yempty = yfull + 2;      // [2] Y rows consumed         dX issuer -> TMA
+  uint64_t* w_full = yempty + 2;     // [2] W buffer written        R-warps -> dX issuer
+  uint64_t* w_empty = w_full + 2;    // [2] W buffer read           dX issuer -> R-warps
+  uint64_t* wt_full = w_empty + 2;   // [2] W^T half written        C-warps -> dY issuer
+  uint64_t* wt_empty = wt_full + 2;  // [2] W^T half read           dY issuer -> C-warps
+  uint64_t* dx_full = wt_empty + 2;  // dX accumulator complete     dX issuer -> R-warps
+  uint64_t* dx_empty = dx_full + 1;  // dX accumulator drained      R-warps -> dX issuer
+  uint64_t* dy_full = dx_empty + 1;  // dY accumulator complete     dY issuer -> C-warps
+  uint64_t* dy_empty = dy_full + 1;  // dY accumulator drained      C-warps -> dY issuer
+  uint64_t* drain = dy_empty + 1;    // teardown of both issuers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < 4; ++s) {
       ptx::mbar_init(&full[s], 1);
-      ptx::mbar_init(&empty[s], 6);  // 4 C-warps + 1 R-warp + 1 MMA commit
+      ptx::mbar_init(&empty[s], 5);  // 4 R-warps + the C-warp of this quadrant
     }
-    for (int b = 0; b < 2; ++b) {
-      ptx::mbar_init(&wt_full[b], 4);
-      ptx::mbar_init(&wt_empty[b], 1);
+    for (int s = 0; s < 2; ++s) {
+      ptx::mbar_init(&xfull[s], 1);
+      ptx::mbar_init(&xempty[s], 1);
+      ptx::mbar_init(&yfull[s], 1);
+      ptx::mbar_init(&yempty[s], 1);
+      ptx::mbar_init(&w_full[s], 4);
+      ptx::mbar_init(&w_empty[s], 1);
+      ptx::mbar_init(&wt_full[s], 4);
+      ptx::mbar_init(&wt_empty[s], 1);
     }
-    ptx::mbar_init(w_full, 4);
     ptx::mbar_init(dx_full, 1);
     ptx::mbar_init(dx_empty, 4);
     ptx::mbar_init(dy_full, 1);
     ptx::mbar_init(dy_empty, 4);
-    ptx::mbar_init(y_full, 1);
-    ptx::mbar_init(y_empty, 1);
-    ptx::mbar_init(drain, 1);
-    for (int s = 0; s < 4; ++s) ptx::mbar_init(&r_full[s], 1);
+    ptx::mbar_init(drain, 2);  // one commit per MMA issuer
     ptx::fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     ptx::prefetch_tensormap(&tm_g);
     ptx::prefetch_tensormap(&tm_k);
-    ptx::prefetch_tensormap(&tm_xhi);
-    ptx::prefetch_tensormap(&tm_xlo);
     ptx::prefetch_tensormap(&tm_yhi);
     ptx::prefetch_tensormap(&tm_ylo);
+    if (a.tma_flush) ptx::prefetch_tensormap(&tm_dx);
   }
-  if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, 512);
+  if (warp == 1 && lane == 0) {
+    ptx::prefetch_tensormap(&tm_xhi);
+    ptx::prefetch_tensormap(&tm_xlo);
+  }
+  if (warp == 2) {
+    ptx::tmem_alloc(tmem_slot, TMEM_COLS);
     ptx::tmem_relinquish();
   }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+#ifdef RBF_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 1024) g_cta_span[blockIdx.x][0] = ptx::globaltimer();
+#endif
 
   // Contiguous, balanced range of tiles for this CTA.
   const int64_t t_begin = a.total_tiles * blockIdx.x / gridDim.x;
   const int64_t t_end = a.total_tiles * (blockIdx.x + 1) / gridDim.x;
 
   if (warp == 0) {
-    // ================================================================ TMA producer
     if (lane == 0) {
-      const uint64_t stream_policy = ptx::policy_evict_first();
-      const uint64_t keep_policy = ptx::policy_evict_last();
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t y_phase = 0;
-      int last_parity[STAGES];
-      for (int s = 0; s < STAGES; ++s) last_parity[s] = -1;
-      int y_issued = -1;
+      // ============================================================ strips of G, K + Y rows
+      const uint64_t stream = ptx::policy_evict_first();
+      const uint64_t keep = ptx::policy_evict_last();
+      uint32_t ph = 0;  // strip stage parity: flips once per tile
+      int yst = 0;
+      uint32_t yph = 0;
+      int last[4] = {-1, -1, -1, -1}, ylast[2] = {-1, -1};
       bool ok = true, skipped = false;
-      int cur_slice = -1, cur_jb = -1;
-      for (int64_t t = t_begin; t < t_end && ok; ++t) {
+      for (int64_t t = t_begin; t < t_end && ok; ++t, ph ^= 1) {
         const TileCoord tc = tile_of(t, a);
         const int i0 = tc.ib * BT, j0 = tc.jb * BT, d0 = tc.slice * DS;
-        if (tc.slice != cur_slice || tc.jb != cur_jb) {
-          cur_slice = tc.slice;
-          cur_jb = tc.jb;
-          // The previous Y tile must be released by the MMAs that read it.
-          if (!ptx::mbar_wait_bounded(y_empty, y_phase ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
-          ptx::mbar_arrive_expect_tx(y_full, 2 * C::Y_BYTES);
+        for (int s = 0; s < 4; ++s) {
+          if (!ptx::mbar_wait_bounded(&empty[s], ph ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
+          TRACE(0, 10 + s);
+          if (a.debug_skip_first_load && !skipped && blockIdx.x == 0) {
+            skipped = true;  // test hook: this strip never arrives, its consumers time out
+          } else {
+            uint8_t* sm = ring + s * 2 * STRIP;
+            ptx::mbar_arrive_expect_tx(&full[s], 2 * STRIP);
+            ptx::tma_load_2d_hint(sm, &tm_g, j0 + SR * s, i0, &full[s], stream);
+            ptx::tma_load_2d_hint(sm + STRIP, &tm_k, j0 + SR * s, i0, &full[s], stream);
+            last[s] = (int)ph;
+          }
+          // Y rows of the strip's 32 columns (B operand of the dX product).
+          if (!ptx::mbar_wait_bounded(&yempty[yst], yph ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
+          uint8_t* ym = yring + yst * 2 * C::X_BYTES;
+          ptx::mbar_arrive_expect_tx(&yfull[yst], 2 * C::X_BYTES);
 #pragma unroll
           for (int b = 0; b < DS / 32; ++b) {
-            ptx::tma_load_2d_hint(ytile + b * C::YBOX, &tm_yhi, d0 + 32 * b, j0, y_full, keep_policy);
-            ptx::tma_load_2d_hint(ytile + C::Y_BYTES + b * C::YBOX, &tm_ylo, d0 + 32 * b, j0,
-                                  y_full, keep_policy);
+            ptx::tma_load_2d_hint(ym + b * BOX, &tm_yhi, d0 + 32 * b, j0 + SR * s, &yfull[yst], keep);
+            ptx::tma_load_2d_hint(ym + C::X_BYTES + b * BOX, &tm_ylo, d0 + 32 * b, j0 + SR * s,
+                                  &yfull[yst], keep);
           }
-          y_issued = (int)y_phase;
-          y_phase ^= 1;
-        }
-        for (int s = 0; s < 4; ++s) {
-          if (!ptx::mbar_wait_bounded(&empty[stage], phase ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
-          if (a.debug_skip_first_load && !skipped && blockIdx.x == 0) {
-            skipped = true;  // test hook: the first strip never arrives
-          } else {
-            uint8_t* sm = ring + stage * C::STAGE_BYTES;
-            uint64_t* fb = &full[stage];
-            ptx::mbar_arrive_expect_tx(fb, C::STAGE_BYTES);
-            const int ir = i0 + SR * s;
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-              ptx::tma_load_2d_hint(sm + b * BOX, &tm_g, j0 + 32 * b, ir, fb, stream_policy);
-              ptx::tma_load_2d_hint(sm + C::G_BYTES + b * BOX, &tm_k, j0 + 32 * b, ir, fb,
-                                    stream_policy);
-            }
-#pragma unroll
-            for (int b = 0; b < DS / 32; ++b) {
-              ptx::tma_load_2d_hint(sm + 2 * C::G_BYTES + b * BOX, &tm_xhi, d0 + 32 * b, ir, fb,
-                                    keep_policy);
-              ptx::tma_load_2d_hint(sm + 2 * C::G_BYTES + C::X_BYTES + b * BOX, &tm_xlo,
-                                    d0 + 32 * b, ir, fb, keep_policy);
-            }
-            last_parity[stage] = (int)phase;
-          }
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          ylast[yst] = (int)yph;
+          if (++yst == YSTAGES) { yst = 0; yph ^= 1; }
         }
       }
-      if (!ok) {
-        for (int s = 0; s < STAGES; ++s)
-          if (last_parity[s] >= 0)
-            ptx::mbar_wait_bounded(&full[s], (uint32_t)last_parity[s], a.status, a.timeout_ns);
-        if (y_issued >= 0) ptx::mbar_wait_bounded(y_full, (uint32_t)y_issued, a.status, a.timeout_ns);
+      if (!ok) {  // let every copy this thread issued land before the CTA exits
+        for (int s = 0; s < 4; ++s)
+          if (last[s] >= 0) ptx::mbar_wait_bounded(&full[s], (uint32_t)last[s], a.status, a.timeout_ns);
+        for (int s = 0; s < 2; ++s)
+          if (ylast[s] >= 0) ptx::mbar_wait_bounded(&yfull[s], (uint32_t)ylast[s], a.status, a.timeout_ns);
       }
     }
   } else if (warp == 1) {
-    // ================================================================ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = ptx::idesc_tf32(128, DS, 0, 1);
-      int stage = 0;
-      uint32_t phase = 0;
-      int wb = 0;
-      uint32_t wt_phase[2] = {0, 0};
-      uint32_t w_phase = 0, dxe_phase = 0, dye_phase = 0, y_phase = 0;
+      // ============================================================ X rows, four chunks per tile
+      const uint64_t keep = ptx::policy_evict_last();
+      int xst = 0;
+      uint32_t xph = 0;
+      int xlast[2] = {-1, -1};
       bool ok = true;
-      int cur_slice = -1, cur_jb = -1;
-      bool dy_first = true;
       for (int64_t t = t_begin; t < t_end && ok; ++t) {
         const TileCoord tc = tile_of(t, a);
-        if (tc.slice != cur_slice || tc.jb != cur_jb) {
-          cur_slice = tc.slice;
-          cur_jb = tc.jb;
-          // dY accumulator drained by the C-warps (flush of the previous segment).
-          if (!ptx::mbar_wait_bounded(dy_empty, dye_phase ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
-          dye_phase ^= 1;
-          if (!ptx::mbar_wait_bounded(y_full, y_phase, a.status, a.timeout_ns)) { ok = false; break; }
-          y_phase ^= 1;
+        const int i0 = tc.ib * BT, d0 = tc.slice * DS;
+        for (int s = 0; s < 4; ++s) {
+          if (!ptx::mbar_wait_bounded(&xempty[xst], xph ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
+          uint8_t* xm = xring + xst * 2 * C::X_BYTES;
+          ptx::mbar_arrive_expect_tx(&xfull[xst], 2 * C::X_BYTES);
+#pragma unroll
+          for (int b = 0; b < DS / 32; ++b) {
+            ptx::tma_load_2d_hint(xm + b * BOX, &tm_xhi, d0 + 32 * b, i0 + SR * s, &xfull[xst], keep);
+            ptx::tma_load_2d_hint(xm + C::X_BYTES + b * BOX, &tm_xlo, d0 + 32 * b, i0 + SR * s,
+                                  &xfull[xst], keep);
+          }
+          xlast[xst] = (int)xph;
+          if (++xst == XSTAGES) { xst = 0; xph ^= 1; }
+        }
+      }
+      if (!ok)
+        for (int s = 0; s < 2; ++s)
+          if (xlast[s] >= 0) ptx::mbar_wait_bounded(&xfull[s], (uint32_t)xlast[s], a.status, a.timeout_ns);
+    }
+  } else if (warp == 2 || warp == 3) {
+    // ================================================================ MMA issuers
+    constexpr uint32_t idesc = ptx::idesc_tf32(128, DS, 0, 1);
+    if (warp == 2 && lane == 0) {
+      // ---- dY: once per tile, A = W^T (TMEM lanes j, K = 128 rows i), B = X rows in 4 chunks.
+      int xs = 0;
+      uint32_t xph = 0, dye_ph = 0;
+      uint32_t wt_ph[2] = {0, 0};
+      bool ok = true, dy_first = true;
+      TileCoord cur = {-1, -1, -1};
+      for (int64_t t = t_begin; t < t_end && ok; ++t) {
+        const TileCoord tc = tile_of(t, a);
+        if (!same_segment(tc, cur)) {
+          cur = tc;
+          // The C-warps drained the dY accumulator of the previous segment.
+          if (!ptx::mbar_wait_bounded(dy_empty, dye_ph ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
+          dye_ph ^= 1;
           dy_first = true;
         }
-        const bool seg_end = segment_ends(t, t_end, tc, a);
-        // ---- dY: one 32-row strip at a time, A = W^T (TMEM lanes j), B = X strip rows.
+        TRACE(2, 10);
         for (int s = 0; s < 4 && ok; ++s) {
-          if (!ptx::mbar_wait_bounded(&wt_full[wb], wt_phase[wb], a.status, a.timeout_ns) ||
-              !ptx::mbar_wait_bounded(&full[stage], phase, a.status, a.timeout_ns)) {
-            ok = false;
-            break;
+          const int h = s >> 1;  // W^T half: rows 64h .. 64h+63
+          if ((s & 1) == 0) {
+            if (!ptx::mbar_wait_bounded(&wt_full[h], wt_ph[h], a.status, a.timeout_ns)) { ok = false; break; }
+            wt_ph[h] ^= 1;
           }
-          wt_phase[wb] ^= 1;
+          if (!ptx::mbar_wait_bounded(&xfull[xs], xph, a.status, a.timeout_ns)) { ok = false; break; }
           ptx::tc_fence_after();
-          const uint32_t xb = ptx::smem_u32(ring + stage * C::STAGE_BYTES + 2 * C::G_BYTES);
-          const uint32_t a_hi = tmem + COL_WT + 64 * wb;
+          const uint32_t xb = ptx::smem_u32(xring + xs * 2 * C::X_BYTES);
+          const uint32_t at = tmem + COL_WT + SR * s;
 #pragma unroll
           for (int k = 0; k < SR / 8; ++k) {
             const uint64_t bh = ptx::smem_desc(xb + 1024 * k, BOX, MN_SBO, MN_LAYOUT);
             const uint64_t bl = ptx::smem_desc(xb + C::X_BYTES + 1024 * k, BOX, MN_SBO, MN_LAYOUT);
-            ptx::mma_tf32_ts(tmem + COL_DY, a_hi + 8 * k, bh, idesc, dy_first ? 0u : 1u);
-            ptx::mma_tf32_ts(tmem + COL_DY, a_hi + 8 * k, bl, idesc, 1);
-            ptx::mma_tf32_ts(tmem + COL_DY, a_hi + 32 + 8 * k, bh, idesc, 1);
+            ptx::mma_tf32_ts(tmem + COL_DY, at + 8 * k, bh, idesc, dy_first ? 0u : 1u);
+            ptx::mma_tf32_ts(tmem + COL_DY, at + 8 * k, bl, idesc, 1);
+            ptx::mma_tf32_ts(tmem + COL_DY, at + 128 + 8 * k, bh, idesc, 1);
             dy_first = false;
           }
-          ptx::mma_commit(&wt_empty[wb]);
-          ptx::mma_commit(&empty[stage]);
-          wb ^= 1;
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          ptx::mma_commit(&xempty[xs]);
+          if (s & 1) ptx::mma_commit(&wt_empty[h]);
+          if (++xs == XSTAGES) { xs = 0; xph ^= 1; }
         }
         if (!ok) break;
-        // ---- dX: A = W (TMEM lanes i, 128 columns of K), B = resident Y tile.
-        if (!ptx::mbar_wait_bounded(w_full, w_phase, a.status, a.timeout_ns) ||
-            !ptx::mbar_wait_bounded(dx_empty, dxe_phase ^ 1, a.status, a.timeout_ns)) {
-          ok = false;
-          break;
+        if (segment_ends(t, t_end, tc, a)) ptx::mma_commit(dy_full);
+      }
+      ptx::mma_commit(drain);  // every MMA this thread issued must finish before TMEM is freed
+      ptx::mbar_wait_bounded(drain, 0, a.status, a.timeout_ns);
+    } else if (warp == 3 && lane == 0) {
+      // ---- dX: per strip, A = W (TMEM lanes i, K = 32 columns j), B = the strip's Y rows.
+      int ys = 0, wb = 0;
+      uint32_t yph = 0, dxe_ph = 0;
+      uint32_t w_ph[2] = {0, 0};
+      bool ok = true;
+      for (int64_t t = t_begin; t < t_end && ok; ++t) {
+        // The R-warps drained the accumulator of the previous tile.
+        if (!ptx::mbar_wait_bounded(dx_empty, dxe_ph ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
+        dxe_ph ^= 1;
+        for (int s = 0; s < 4 && ok; ++s) {
+          if (!ptx::mbar_wait_bounded(&w_full[wb], w_ph[wb], a.status, a.timeout_ns) ||
+              !ptx::mbar_wait_bounded(&yfull[ys], yph, a.status, a.timeout_ns)) { ok = false; break; }
+          w_ph[wb] ^= 1;
+          TRACE(2, 20 + s);
+          ptx::tc_fence_after();
+          const uint32_t aw = tmem + COL_W + 64 * wb;
+          const uint32_t yb = ptx::smem_u32(yring + ys * 2 * C::X_BYTES);
+#pragma unroll
+          for (int k = 0; k < SR / 8; ++k) {
+            const uint64_t bh = ptx::smem_desc(yb + 1024 * k, BOX, MN_SBO, MN_LAYOUT);
+            const uint64_t bl = ptx::smem_desc(yb + C::X_BYTES + 1024 * k, BOX, MN_SBO, MN_LAYOUT);
+            ptx::mma_tf32_ts(tmem + COL_DX, aw + 8 * k, bh, idesc, (s | k) != 0 ? 1u : 0u);
+            ptx::mma_tf32_ts(tmem + COL_DX, aw + 8 * k, bl, idesc, 1);
+            ptx::mma_tf32_ts(tmem + COL_DX, aw + 32 + 8 * k, bh, idesc, 1);
+          }
+          ptx::mma_commit(&w_empty[wb]);
+          ptx::mma_commit(&yempty[ys]);
+          wb ^= 1;
+          if (++ys == YSTAGES) { ys = 0; yph ^= 1; }
         }
-        w_phase ^= 1;
-        dxe_phase ^= 1;
-        ptx::tc_fence_after();
-        const uint32_t yb = ptx::smem_u32(ytile);
-#pragma unroll 4
-        for (int k = 0; k < BT / 8; ++k) {
-          const uint64_t bh = ptx::smem_desc(yb + 1024 * k, C::YBOX, MN_SBO, MN_LAYOUT);
-          const uint64_t bl = ptx::smem_desc(yb + C::Y_BYTES + 1024 * k, C::YBOX, MN_SBO, MN_LAYOUT);
-          ptx::mma_tf32_ts(tmem + COL_DX, tmem + COL_W + 8 * k, bh, idesc, k > 0 ? 1u : 0u);
-          ptx::mma_tf32_ts(tmem + COL_DX, tmem + COL_W + 8 * k, bl, idesc, 1);
-          ptx::mma_tf32_ts(tmem + COL_DX, tmem + COL_W + 128 + 8 * k, bh, idesc, 1);
-        }
+        if (!ok) break;
         ptx::mma_commit(dx_full);
-        if (seg_end) {
-          ptx::mma_commit(dy_full);
-          ptx::mma_commit(y_empty);
-        }
       }
       ptx::mma_commit(drain);
       ptx::mbar_wait_bounded(drain, 0, a.status, a.timeout_ns);
     }
-  } else if (warp < 6) {
+  } else if (warp < 8) {
     // ================================================================ C-warps (column j)
+    // C-warp q reads strip q (its 32 columns, all 128 rows) and writes W^T for them, in two
+    // halves of 64 rows so that one half is refilled while the dY MMAs read the other.
     const int q = warp & 3;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    int stage = 0;
-    uint32_t phase = 0;
-    int wb = 0;
-    uint32_t wte_phase[2] = {0, 0};
-    uint32_t dyf_phase = 0;
+    uint32_t ph = 0, dyf_ph = 0;
+    uint32_t wte_ph[2] = {0, 0};
     float colsum = 0.f;
-    int cur_slice = -1, cur_jb = -1;
+    TileCoord cur = {-1, -1, -1};
     bool ok = true;
-    for (int64_t t = t_begin; t < t_end && ok; ++t) {
+    // Byte offset of this lane's column inside a 128-byte swizzled row, for row % 8 = r.
+    uint32_t coff[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) coff[r] = (((lane >> 2) ^ r) << 4) + (lane & 3) * 4;
+    for (int64_t t = t_begin; t < t_end && ok; ++t, ph ^= 1) {
       const TileCoord tc = tile_of(t, a);
-      if (tc.slice != cur_slice || tc.jb != cur_jb) {
-        cur_slice = tc.slice;
-        cur_jb = tc.jb;
+      if (!same_segment(tc, cur)) {
+        cur = tc;
         colsum = 0.f;
       }
-      const bool seg_end = segment_ends(t, t_end, tc, a);
-      for (int s = 0; s < 4; ++s) {
-        if (!ptx::mbar_wait_bounded(&full[stage], phase, a.status, a.timeout_ns)) { ok = false; break; }
-        // Hand strip s to R-warp s.  The R-warps cannot wait on full[] themselves: strip 3 sits
-        // in a stage one phase ahead of strips 0-2, and a parity wait cannot tell the phases
-        // apart.  r_full[s] advances exactly once per tile, so its parity is unambiguous.
-        if (q == 0 && lane == 0) ptx::mbar_arrive(&r_full[s]);
-        const uint8_t* sm = ring + stage * C::STAGE_BYTES;
-        const uint8_t* gb = sm + q * BOX;
-        const uint8_t* kb = sm + C::G_BYTES + q * BOX;
-        uint32_t hi[32], lo[32];
-        const int ch = lane >> 2, wi = (lane & 3) * 4;
-#pragma unroll
-        for (int r = 0; r < 32; ++r) {
-          const int off = r * 128 + ((ch ^ (r & 7)) << 4) + wi;
-          const float w = *reinterpret_cast<const float*>(gb + off) *
-                          *reinterpret_cast<const float*>(kb + off);
-          colsum += w;
-          float h, l;
-          tf32_split(w, h, l);
-          hi[r] = __float_as_uint(h);
-          lo[r] = __float_as_uint(l);
-        }
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&empty[stage]);
-        if (!ptx::mbar_wait_bounded(&wt_empty[wb], wte_phase[wb] ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
-        wte_phase[wb] ^= 1;
+      if (!ptx::mbar_wait_bounded(&full[q], ph, a.status, a.timeout_ns)) { ok = false; break; }
+      if (lane == 0 && q == 0) TRACE(3, 10);
+      const uint8_t* gb = ring + q * 2 * STRIP;
+      const uint8_t* kb = gb + STRIP;
+#pragma unroll 1
+      for (int h = 0; h < 2 && ok; ++h) {
+        // This half of the W^T tile was read by the previous tile's dY MMAs.
+        if (!ptx::mbar_wait_bounded(&wt_empty[h], wte_ph[h] ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
+        wte_ph[h] ^= 1;
         ptx::tc_fence_after();
-        ptx::tmem_st32(tmem + lane_base + COL_WT + 64 * wb, hi);
-        ptx::tmem_st32(tmem + lane_base + COL_WT + 64 * wb + 32, lo);
+#pragma unroll 1
+        for (int r0 = 64 * h; r0 < 64 * h + 64; r0 += 32) {
+          uint32_t hi[32], lo[32];
+#pragma unroll
+          for (int r = 0; r < 32; ++r) {
+            const uint32_t off = (uint32_t)(r0 + r) * 128 + coff[r & 7];
+            const float w = *reinterpret_cast<const float*>(gb + off) *
+                            *reinterpret_cast<const float*>(kb + off);
+            colsum += w;
+            float hh, ll;
+            tf32_split(w, hh, ll);
+            hi[r] = __float_as_uint(hh);
+            lo[r] = __float_as_uint(ll);
+          }
+          ptx::tmem_st32(tmem + lane_base + COL_WT + r0, hi);
+          ptx::tmem_st32(tmem + lane_base + COL_WT + 128 + r0, lo);
+        }
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&wt_full[wb]);
-        wb ^= 1;
-        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        if (lane == 0) ptx::mbar_arrive(&wt_full[h]);
       }
       if (!ok) break;
-      if (seg_end) {
-        if (!ptx::mbar_wait_bounded(dy_full, dyf_phase, a.status, a.timeout_ns)) { ok = false; break; }
-        dyf_phase ^= 1;
+      if (lane == 0) ptx::mbar_arrive(&empty[q]);
+      if (lane == 0 && q == 0) TRACE(3, 30);
+      if (segment_ends(t, t_end, tc, a)) {
+        if (!ptx::mbar_wait_bounded(dy_full, dyf_ph, a.status, a.timeout_ns)) { ok = false; break; }
+        dyf_ph ^= 1;
         ptx::tc_fence_after();
-        uint32_t acc[64];
-        tmem_load_row<DS>(tmem + lane_base + COL_DY, acc);
+        uint32_t accv[64];
+        tmem_load_row<DS>(tmem + lane_base + COL_DY, accv);
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(dy_empty);
         const int64_t j = (int64_t)tc.jb * BT + q * 32 + lane;
-        if (j < a.M) flush_row<DS>(a.dY, a.Y, j, a.D, tc.slice * DS, a.c, colsum, acc);
+        if (j < a.M) flush_row<DS>(a.dY, a.Y, j, a.D, tc.slice * DS, a.c, colsum, accv);
       }
     }
   } else {
     // ================================================================ R-warps (row i)
-    const int q = warp & 3;  // this warp's strip within the tile and its TMEM lane quadrant
+    // Tile t's dX accumulator is drained and flushed right after the first strip of tile t+1
+    // is handed over, so the flush never stalls the conversion -> MMA chain for long.
+    const int q = warp & 3;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    int64_t strip_count = 0;  // strips consumed by this CTA so far (ring position)
-    uint32_t dxf_phase = 0, rf_phase = 0;
-    bool ok = true;
-    for (int64_t t = t_begin; t < t_end && ok; ++t, strip_count += 4) {
-      const TileCoord tc = tile_of(t, a);
-      const int64_t pos = strip_count + q;
-      const int stage = (int)(pos % STAGES);
-      if (!ptx::mbar_wait_bounded(&r_full[q], rf_phase, a.status, a.timeout_ns)) { ok = false; break; }
-      rf_phase ^= 1;
-      const uint8_t* sm = ring + stage * C::STAGE_BYTES;
-      float rowsum = 0.f;
-      // The W buffer is free: this warp waited for the previous tile's dX MMAs (dx_full).
+    int wb = 0;
+    uint32_t ph = 0, dxf_ph = 0;
+    uint32_t we_ph[2] = {0, 0};
+    bool ok = true, pending = false;
+    float prev_rowsum = 0.f;
+    int64_t prev_i = 0;
+    int prev_d0 = 0;
+    auto flush_prev = [&]() -> bool {
+      if (!ptx::mbar_wait_bounded(dx_full, dxf_ph, a.status, a.timeout_ns)) return false;
+      dxf_ph ^= 1;
       ptx::tc_fence_after();
-#pragma unroll 1
-      for (int b = 0; b < 4; ++b) {
-        const uint8_t* gb = sm + b * BOX + lane * 128;
-        const uint8_t* kb = sm + C::G_BYTES + b * BOX + lane * 128;
+      uint32_t accv[64];
+      tmem_load_row<DS>(tmem + lane_base + COL_DX, accv);
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(dx_empty);
+      if (!a.tma_flush) {
+        if (prev_i < a.N) flush_row<DS>(a.dX, a.X, prev_i, a.D, prev_d0, a.c, prev_rowsum, accv);
+        return true;
+      }
+      // -c * acc goes through shared memory to a TMA reduce-add (32 rows x DS, coalesced in L2);
+      // c * rowsum * x is added once per row by the finalize pass from the rowsum vector.
+      if (prev_i < a.N && prev_d0 == 0 && !(a.ablate & 2)) red_add1(a.rowsum + prev_i, prev_rowsum);
+      uint8_t* stg = staging + q * C::STAGING;
+      if (lane == 0) ptx::bulk_wait_read<0>();  // the previous reduce has read the buffer
+      __syncwarp();
+#pragma unroll
+      for (int bx = 0; bx < DS / 32; ++bx) {
+        uint8_t* row = stg + bx * BOX + lane * 128;
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const uint32_t* v = accv + 32 * bx + 4 * c4;
+          *reinterpret_cast<float4*>(row + ((c4 ^ (lane & 7)) << 4)) =
+              make_float4(-a.c * __uint_as_float(v[0]), -a.c * __uint_as_float(v[1]),
+                          -a.c * __uint_as_float(v[2]), -a.c * __uint_as_float(v[3]));
+        }
+      }
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && !(a.ablate & 1)) {
+#pragma unroll
+        for (int bx = 0; bx < DS / 32; ++bx)
+          ptx::tma_reduce_add_2d(&tm_dx, stg + bx * BOX, prev_d0 + 32 * bx, (int)prev_i);
+        ptx::bulk_commit();
+      }
+      return true;
+    };
+    for (int64_t t = t_begin; t < t_end && ok; ++t, ph ^= 1) {
+      const TileCoord tc = tile_of(t, a);
+      float rowsum = 0.f;
+      for (int s = 0; s < 4; ++s) {
+        if (!ptx::mbar_wait_bounded(&full[s], ph, a.status, a.timeout_ns)) { ok = false; break; }
+        if (lane == 0 && q == 0) TRACE(4, 10 + s);
+        // Row (32q + lane) of strip s: its 32 columns in 128 swizzled bytes.
+        const uint8_t* gb = ring + s * 2 * STRIP + (q * 32 + lane) * 128;
+        const uint8_t* kb = gb + STRIP;
         uint32_t hi[32], lo[32];
 #pragma unroll
         for (int c4 = 0; c4 < 8; ++c4) {
@@ -462,39 +566,72 @@ __global__ void __launch_bounds__(THREADS, 1)
             lo[4 * c4 + e] = __float_as_uint(l);
           }
         }
-        ptx::tmem_st32(tmem + lane_base + COL_W + 32 * b, hi);
-        ptx::tmem_st32(tmem + lane_base + COL_W + 128 + 32 * b, lo);
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&empty[s]);
+        if (!ptx::mbar_wait_bounded(&w_empty[wb], we_ph[wb] ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
+        we_ph[wb] ^= 1;
+        ptx::tc_fence_after();
+        ptx::tmem_st32(tmem + lane_base + COL_W + 64 * wb, hi);
+        ptx::tmem_st32(tmem + lane_base + COL_W + 64 * wb + 32, lo);
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&w_full[wb]);
+        if (lane == 0 && q == 0) TRACE(4, 30 + s);
+        wb ^= 1;
+        if (s == 0 && pending) {
+          if (!flush_prev()) { ok = false; break; }
+          pending = false;
+          if (lane == 0 && q == 0) TRACE(4, 40);
+        }
       }
-      ptx::tmem_wait_st();
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        ptx::mbar_arrive(&empty[stage]);
-        ptx::mbar_arrive(w_full);
-      }
-      // dX of this tile: wait for the MMAs, drain the accumulator, flush.
-      if (!ptx::mbar_wait_bounded(dx_full, dxf_phase, a.status, a.timeout_ns)) { ok = false; break; }
-      dxf_phase ^= 1;
-      ptx::tc_fence_after();
-      uint32_t acc[64];
-      tmem_load_row<DS>(tmem + lane_base + COL_DX, acc);
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(dx_empty);
-      const int64_t i = (int64_t)tc.ib * BT + q * 32 + lane;
-      if (i < a.N) flush_row<DS>(a.dX, a.X, i, a.D, tc.slice * DS, a.c, rowsum, acc);
+      if (!ok) break;
+      pending = true;
+      prev_rowsum = rowsum;
+      prev_i = (int64_t)tc.ib * BT + q * 32 + lane;
+      prev_d0 = tc.slice * DS;
     }
+    if (ok && pending) flush_prev();
+    if (lane == 0) ptx::bulk_wait<0>();  // reduces complete before the CTA exits
   }
 
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+#ifdef RBF_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 1024) g_cta_span[blockIdx.x][1] = ptx::globaltimer();
+#endif
+  if (warp == 2) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem, 512);
+    ptx::tmem_dealloc(tmem, TMEM_COLS);
   }
 }
 
+// dX[i,:] += c * rowsum[i] * X[i,:]: the part of every tile's dX flush that the TMA reduce
+// leaves out (one pass over dX instead of one per tile).  One thread per 4 features.
+__global__ void __launch_bounds__(256) rbf_bwd_finalize_kernel(const float* __restrict__ X,
+                                                               const float* __restrict__ rowsum,
+                                                               float* __restrict__ dX, int64_t N,
+                                                               int64_t D, float c) {
+  const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // float4 index
+  const int64_t per_row = D / 4;
+  if (q >= N * per_row) return;
+  const int64_t i = q / per_row;
+  const float s = c * rowsum[i];
+  const float4 x = __ldg(reinterpret_cast<const float4*>(X) + q);
+  float4 v = reinterpret_cast<float4*>(dX)[q];
+  v.x = fmaf(s, x.x, v.x);
+  v.y = fmaf(s, x.y, v.y);
+  v.z = fmaf(s, x.z, v.z);
+  v.w = fmaf(s, x.w, v.w);
+  reinterpret_cast<float4*>(dX)[q] = v;
+}
+
 }  // namespace
+
+size_t backward_scratch_bytes(int64_t N, int64_t M, int64_t D) {
+  (void)M; (void)D;
+  return (size_t)round_up((int64_t)sizeof(float) * N, (int64_t)kAlign);
+}
 
 bool backward_tc_supported(int64_t N, int64_t M, int64_t D) {
   (void)N; (void)D;
@@ -511,18 +648,28 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
   const PrepLayout L = prep_layout(N, M, D);
   const int DS = (D <= 32) ? 32 : 64;
   const int mn = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
-  CUtensorMap tg, tk, txh, txl, tyh, tyl;
-  if (!make_tmap_2d(&tg, G, N, M, M, 32, 32) || !make_tmap_2d(&tk, K, N, M, M, 32, 32) ||
+  const bool tma_flush = (D % 4) == 0;  // dX rows 16-byte pitched
+  float* rowsum = ws_at<float>(ws, L.end);
+  CUtensorMap tg, tk, txh, txl, tyh, tyl, tdx;
+  if (!make_tmap_2d(&tg, G, N, M, M, 32, 128) || !make_tmap_2d(&tk, K, N, M, M, 32, 128) ||
       !make_tmap_2d(&txh, ws_at<float>(ws, L.xhi), N, L.Dp, L.Dp, 32, 32, mn) ||
       !make_tmap_2d(&txl, ws_at<float>(ws, L.xlo), N, L.Dp, L.Dp, 32, 32, mn) ||
-      !make_tmap_2d(&tyh, ws_at<float>(ws, L.yhi), M, L.Dp, L.Dp, 32, 128, mn) ||
-      !make_tmap_2d(&tyl, ws_at<float>(ws, L.ylo), M, L.Dp, L.Dp, 32, 128, mn))
+      !make_tmap_2d(&tyh, ws_at<float>(ws, L.yhi), M, L.Dp, L.Dp, 32, 32, mn) ||
+      !make_tmap_2d(&tyl, ws_at<float>(ws, L.ylo), M, L.Dp, L.Dp, 32, 32, mn))
     return cudaErrorInvalidValue;
+  if (tma_flush) {
+    if (!make_tmap_2d(&tdx, dX, N, D, D, 32, 32)) return cudaErrorInvalidValue;
+    if ((e = cudaMemsetAsync(rowsum, 0, sizeof(float) * (size_t)N, stream)) != cudaSuccess) return e;
+  } else {
+    tdx = tg;  // unused
+  }
   BwdArgs a;
   a.X = X;
   a.Y = Y;
   a.dX = dX;
   a.dY = dY;
+  a.rowsum = rowsum;
+  a.tma_flush = tma_flush ? 1 : 0;
   a.N = N;
   a.M = M;
   a.D = D;
@@ -534,20 +681,47 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
   a.status = ws_at<int>(ws, L.status);
   a.timeout_ns = wc.timeout_ns;
   a.debug_skip_first_load = wc.debug_skip_first_load;
+  a.ablate = 0;
+#ifdef RBF_TRACE
+  if (const char* ab = std::getenv("RBF_ABLATE")) a.ablate = std::atoi(ab);
+#endif
   const int grid = (int)std::min<int64_t>(a.total_tiles, device_sm_count());
   if (DS == 32) {
     if ((e = cudaFuncSetAttribute(rbf_bwd_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)Cfg<32>::SMEM)) != cudaSuccess)
       return e;
-    rbf_bwd_tc_kernel<32><<<grid, THREADS, Cfg<32>::SMEM, stream>>>(tg, tk, txh, txl, tyh, tyl, a);
+    rbf_bwd_tc_kernel<32><<<grid, THREADS, Cfg<32>::SMEM, stream>>>(tg, tk, txh, txl, tyh, tyl,
+                                                                   tdx, a);
   } else {
     if ((e = cudaFuncSetAttribute(rbf_bwd_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)Cfg<64>::SMEM)) != cudaSuccess)
       return e;
-    rbf_bwd_tc_kernel<64><<<grid, THREADS, Cfg<64>::SMEM, stream>>>(tg, tk, txh, txl, tyh, tyl, a);
+    rbf_bwd_tc_kernel<64><<<grid, THREADS, Cfg<64>::SMEM, stream>>>(tg, tk, txh, txl, tyh, tyl,
+                                                                   tdx, a);
   }
   note_launches(1);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if (tma_flush) {
+    const int64_t n4 = N * (D / 4);
+    rbf_bwd_finalize_kernel<<<(unsigned)ceil_div(n4, 256), 256, 0, stream>>>(X, rowsum, dX, N, D,
+                                                                             a.c);
+    note_launches(1);
+  }
   return cudaGetLastError();
 }
 
 }  // namespace rbf
+
+#ifdef RBF_TRACE
+extern "C" __attribute__((visibility("default"))) int rbf_debug_trace(unsigned long long* out,
+                                                                      int* n) {
+  cudaMemcpyFromSymbol(out, rbf::g_trace, sizeof(rbf::g_trace));
+  cudaMemcpyFromSymbol(n, rbf::g_trace_n, sizeof(rbf::g_trace_n));
+  int z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  return (int)cudaMemcpyToSymbol(rbf::g_trace_n, z, sizeof(z));
+}
+
+extern "C" __attribute__((visibility("default"))) int rbf_debug_spans(unsigned long long* out) {
+  return (int)cudaMemcpyFromSymbol(out, rbf::g_cta_span, sizeof(rbf::g_cta_span));
+}
+#endif

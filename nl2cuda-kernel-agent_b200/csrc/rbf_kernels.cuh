@@ -35,6 +35,8 @@ int device_sm_count();
 // rbf_bwd_tc.cu: the fused tcgen05 3xTF32 backward (zeroes dX, dY, then accumulates into
 // them).  Needs M % 4 == 0 (16-byte pitched rows of G and K for TMA).
 bool backward_tc_supported(int64_t N, int64_t M, int64_t D);
+// Workspace bytes the tensor-core backward needs after the split-pass layout (rowsum vector).
+size_t backward_scratch_bytes(int64_t N, int64_t M, int64_t D);
 cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, const float* K,
                                float* dX, float* dY, int64_t N, int64_t M, int64_t D,
                                float gamma, void* ws, const WaitConfig& wc, cudaStream_t stream);
