@@ -366,9 +366,16 @@ def main():
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+    # Graphs that captured NCCL work must be gone before the communicator is; the process then
+    # exits without tearing the process group down (destroying it while captured collectives
+    # existed hung on this pool).
+    del step_graph, fwd_graph, bwd_graph
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-        dist.destroy_process_group()
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(0)
 
 
 def run_e2e(X, Y, G, g, world, dev, args, shard, op):
