@@ -252,7 +252,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 #ifdef RBF_TRACE
-  if (threadIdx.x == 0 && blockIdx.x < 1024) g_cta_span[blockIdx.x][0] = ptx::globaltimer();
+  if (threadIdx.x == 0 && blockIdx.x < 1024) g_cta_span[blockIdx.x][0] = ptx::globaltimer() & ((1ull << 48) - 1);
 #endif
 
   // Contiguous, balanced range of tiles for this CTA.
@@ -598,7 +598,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   ptx::tc_fence_before();
   __syncthreads();
 #ifdef RBF_TRACE
-  if (threadIdx.x == 0 && blockIdx.x < 1024) g_cta_span[blockIdx.x][1] = ptx::globaltimer();
+  if (threadIdx.x == 0 && blockIdx.x < 1024) {
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    g_cta_span[blockIdx.x][1] = (ptx::globaltimer() & ((1ull << 48) - 1)) | ((unsigned long long)smid << 48);
+  }
 #endif
   if (warp == 2) {
     ptx::tc_fence_after();

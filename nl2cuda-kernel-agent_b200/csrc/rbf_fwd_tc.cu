@@ -10,13 +10,14 @@
 //
 // Kernel organisation (one persistent CTA per SM, 320 threads):
 //   warp 0    TMA producer: per stage one 32-feature slice of Xhi, Xlo (128 rows each) and of
-//             Yhi, Ylo (128 rows each), 128-byte swizzled, into a 3-deep ring (64 KiB/stage).
+//             Yhi, Ylo (128 rows each), 128-byte swizzled, into a 2-deep ring (64 KiB/stage).
 //   warp 1    MMA issuer (one thread): 3 x tcgen05.mma.kind::tf32 (M=128, N=128, K=8) per 8
 //             features into one of two TMEM accumulators (2 x 128 columns), so the epilogue of
 //             tile t overlaps the MMAs of tile t+1.
 //   warps 2-9 epilogue: warp w reads TMEM lanes 32*(w%4).. (its row quadrant) and one half of
 //             the columns, adds the norms, clamps, exponentiates (MUFU ex2), stages 32x32 fp32
-//             blocks in swizzled shared memory and writes them with TMA stores (no multicast).
+//             blocks in swizzled shared memory (two per warp, so a chunk never waits for the
+//             previous store to drain) and writes them with TMA stores (no multicast).
 // Every mbarrier wait is bounded (globaltimer); on expiry the kernel records RBF_ERR_TIMEOUT in
 // the workspace status word, waits (bounded) for its own copies in flight, frees TMEM and
 // returns.
@@ -36,15 +37,23 @@ namespace {
 constexpr int BM = 128;
 constexpr int BN = 128;
 constexpr int BK = 32;
-constexpr int STAGES = 3;
+constexpr int STAGES = 2;
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 32 * (2 + EPI_WARPS);
 constexpr uint32_t TILE_BYTES = 128 * BK * 4;  // 16 KiB: 128 rows x 128 bytes
 constexpr uint32_t STAGE_BYTES = 4 * TILE_BYTES;
-constexpr uint32_t EPI_BYTES = 32 * 32 * 4;    // one 32x32 fp32 staging block per warp
+constexpr uint32_t EPI_BYTES = 2 * 32 * 32 * 4;  // two 32x32 fp32 staging blocks per warp
 constexpr uint32_t TMEM_COLS = 2 * BN;
 constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + EPI_WARPS * EPI_BYTES + 256;
 static_assert(SMEM_BYTES <= 232448, "forward shared memory over the sm_100 limit");
+// Resident-X variant (D <= 64, at most two 32-feature chunks): the CTA walks its tiles along j,
+// so the X hi/lo slices of one row block stay in shared memory and only Y is streamed.
+constexpr int RA_CHUNKS = 2;
+constexpr int RB_STAGES = 3;
+constexpr uint32_t CHUNK_BYTES = 2 * TILE_BYTES;  // hi + lo of one 32-feature slice, 128 rows
+constexpr size_t SMEM_BYTES_RA =
+    1024 + (size_t)RA_CHUNKS * CHUNK_BYTES + RB_STAGES * CHUNK_BYTES + EPI_WARPS * EPI_BYTES + 256;
+static_assert(SMEM_BYTES_RA <= 232448, "forward shared memory over the sm_100 limit");
 
 struct FwdArgs {
   const float* xn;
@@ -58,7 +67,7 @@ struct FwdArgs {
   int debug_skip_first_load;
 };
 
-template <bool TMA_STORE>
+template <bool TMA_STORE, bool RES_A>
 __global__ void __launch_bounds__(THREADS, 1)
     rbf_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_xhi,
                       const __grid_constant__ CUtensorMap tm_xlo,
@@ -68,12 +77,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
+  // Streamed variant: [STAGES][X hi | X lo | Y hi | Y lo].  Resident-X variant:
+  // [RA_CHUNKS][X hi | X lo] then [RB_STAGES][Y hi | Y lo].
   uint8_t* stage_mem = smem;
-  uint8_t* epi_mem = smem + STAGES * STAGE_BYTES;
+  uint8_t* epi_mem = smem + (RES_A ? (RA_CHUNKS + RB_STAGES) * CHUNK_BYTES : STAGES * STAGE_BYTES);
   uint64_t* bars = reinterpret_cast<uint64_t*>(epi_mem + EPI_WARPS * EPI_BYTES);
-  uint64_t* full = bars;                  // [STAGES]  TMA -> MMA
-  uint64_t* empty = bars + STAGES;        // [STAGES]  MMA -> TMA
-  uint64_t* acc_full = bars + 2 * STAGES; // [2]       MMA -> epilogue
+  uint64_t* full = bars;                  // [4]  TMA -> MMA (operand stage)
+  uint64_t* empty = bars + 4;             // [4]  MMA -> TMA
+  uint64_t* a_full = bars + 8;            // resident X landed   TMA -> MMA
+  uint64_t* a_empty = bars + 9;           // resident X released MMA -> TMA
+  uint64_t* acc_full = bars + 10;         // [2]       MMA -> epilogue
   uint64_t* acc_empty = acc_full + 2;     // [2]       epilogue -> MMA
   uint64_t* drain = acc_empty + 2;        // [1]       MMA teardown
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -81,10 +94,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < 4; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
     }
+    ptx::mbar_init(a_full, 1);
+    ptx::mbar_init(a_empty, 1);
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(&acc_full[b], 1);
       ptx::mbar_init(&acc_empty[b], EPI_WARPS);
@@ -107,20 +122,66 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int num_tiles = a.tiles_m * a.tiles_n;
+  // Contiguous, balanced tile range per CTA; tiles run along j (t -> ib = t / tiles_n).
+  const int64_t num_tiles = (int64_t)a.tiles_m * a.tiles_n;
+  const int64_t t_begin = num_tiles * blockIdx.x / gridDim.x;
+  const int64_t t_end = num_tiles * (blockIdx.x + 1) / gridDim.x;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
+    if (lane == 0 && RES_A) {
+      constexpr int NS = RB_STAGES;
+      int stage = 0;
+      uint32_t phase = 0, a_phase = 0;
+      int last_parity[NS], a_issued = -1;
+      for (int s = 0; s < NS; ++s) last_parity[s] = -1;
+      bool ok = true, skipped = false;
+      int cur_ib = -1;
+      for (int64_t t = t_begin; t < t_end && ok; ++t) {
+        const int ib = (int)(t / a.tiles_n);
+        const int i0 = ib * BM, j0 = (int)(t % a.tiles_n) * BN;
+        if (ib != cur_ib) {
+          cur_ib = ib;
+          if (!ptx::mbar_wait_bounded(a_empty, a_phase ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
+          ptx::mbar_arrive_expect_tx(a_full, (uint32_t)a.num_kc * CHUNK_BYTES);
+          for (int kc = 0; kc < a.num_kc; ++kc) {
+            uint8_t* am = stage_mem + kc * CHUNK_BYTES;
+            ptx::tma_load_2d(am, &tm_xhi, kc * BK, i0, a_full);
+            ptx::tma_load_2d(am + TILE_BYTES, &tm_xlo, kc * BK, i0, a_full);
+          }
+          a_issued = (int)a_phase;
+          a_phase ^= 1;
+        }
+        for (int kc = 0; kc < a.num_kc; ++kc) {
+          if (!ptx::mbar_wait_bounded(&empty[stage], phase ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
+          if (a.debug_skip_first_load && !skipped && blockIdx.x == 0) {
+            skipped = true;  // test hook: this stage never fills, so its consumer times out
+          } else {
+            uint8_t* bm = stage_mem + (RA_CHUNKS + stage) * CHUNK_BYTES;
+            ptx::mbar_arrive_expect_tx(&full[stage], CHUNK_BYTES);
+            ptx::tma_load_2d(bm, &tm_yhi, kc * BK, j0, &full[stage]);
+            ptx::tma_load_2d(bm + TILE_BYTES, &tm_ylo, kc * BK, j0, &full[stage]);
+            last_parity[stage] = (int)phase;
+          }
+          if (++stage == NS) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {  // let every load this thread issued land before the CTA exits
+        for (int s = 0; s < NS; ++s)
+          if (last_parity[s] >= 0)
+            ptx::mbar_wait_bounded(&full[s], (uint32_t)last_parity[s], a.status, a.timeout_ns);
+        if (a_issued >= 0) ptx::mbar_wait_bounded(a_full, (uint32_t)a_issued, a.status, a.timeout_ns);
+      }
+    } else if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int last_parity[STAGES];
       for (int s = 0; s < STAGES; ++s) last_parity[s] = -1;
       bool ok = true;
       bool skipped = false;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int i0 = (t % a.tiles_m) * BM;
-        const int j0 = (t / a.tiles_m) * BN;
+      for (int64_t t = t_begin; t < t_end && ok; ++t) {
+        const int i0 = (int)(t / a.tiles_n) * BM;
+        const int j0 = (int)(t % a.tiles_n) * BN;
         for (int kc = 0; kc < a.num_kc; ++kc) {
           if (!ptx::mbar_wait_bounded(&empty[stage], phase ^ 1, a.status, a.timeout_ns)) {
             ok = false;
@@ -154,12 +215,20 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = ptx::idesc_tf32(BM, BN, 0, 0);
+      constexpr int NS = RES_A ? RB_STAGES : STAGES;
       int stage = 0;
-      uint32_t phase = 0;
+      uint32_t phase = 0, a_phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      int cur_ib = -1;
+      for (int64_t t = t_begin; t < t_end && ok; ++t) {
+        const int ib = (int)(t / a.tiles_n);
+        if (RES_A && ib != cur_ib) {
+          cur_ib = ib;
+          if (!ptx::mbar_wait_bounded(a_full, a_phase, a.status, a.timeout_ns)) { ok = false; break; }
+          a_phase ^= 1;
+        }
         if (!ptx::mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1, a.status, a.timeout_ns)) {
           ok = false;
           break;
@@ -172,26 +241,32 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           ptx::tc_fence_after();
-          const uint32_t base = ptx::smem_u32(stage_mem + stage * STAGE_BYTES);
+          // Operand bases: A = X hi|lo, B = Y hi|lo of this K chunk.
+          const uint32_t abase = RES_A ? ptx::smem_u32(stage_mem + kc * CHUNK_BYTES)
+                                       : ptx::smem_u32(stage_mem + stage * STAGE_BYTES);
+          const uint32_t bbase = RES_A ? ptx::smem_u32(stage_mem + (RA_CHUNKS + stage) * CHUNK_BYTES)
+                                       : abase + 2 * TILE_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 8; ++k) {
             const uint32_t off = (uint32_t)k * 32;  // 8 tf32 = 32 bytes along the swizzled row
-            const uint64_t ahi = ptx::smem_desc(base + off, 16, 1024, 2);
-            const uint64_t alo = ptx::smem_desc(base + TILE_BYTES + off, 16, 1024, 2);
-            const uint64_t bhi = ptx::smem_desc(base + 2 * TILE_BYTES + off, 16, 1024, 2);
-            const uint64_t blo = ptx::smem_desc(base + 3 * TILE_BYTES + off, 16, 1024, 2);
+            const uint64_t ahi = ptx::smem_desc(abase + off, 16, 1024, 2);
+            const uint64_t alo = ptx::smem_desc(abase + TILE_BYTES + off, 16, 1024, 2);
+            const uint64_t bhi = ptx::smem_desc(bbase + off, 16, 1024, 2);
+            const uint64_t blo = ptx::smem_desc(bbase + TILE_BYTES + off, 16, 1024, 2);
             ptx::mma_tf32_ss(d, ahi, bhi, idesc, (kc | k) != 0);
             ptx::mma_tf32_ss(d, ahi, blo, idesc, 1);
             ptx::mma_tf32_ss(d, alo, bhi, idesc, 1);
           }
           ptx::mma_commit(&empty[stage]);
-          if (++stage == STAGES) {
+          if (++stage == NS) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
         ptx::mma_commit(&acc_full[acc]);
+        // Last tile of this row block: the resident X may be replaced once these MMAs finish.
+        if (RES_A && (t + 1 == t_end || (int)((t + 1) / a.tiles_n) != ib)) ptx::mma_commit(a_empty);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;
@@ -208,9 +283,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t* buf = epi_mem + (warp - 2) * EPI_BYTES;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-      const int64_t i0 = (int64_t)(t % a.tiles_m) * BM;
-      const int64_t j0 = (int64_t)(t / a.tiles_m) * BN;
+    for (int64_t t = t_begin; t < t_end; ++t) {
+      const int64_t i0 = (t / a.tiles_n) * BM;
+      const int64_t j0 = (t % a.tiles_n) * BN;
       if (!ptx::mbar_wait_bounded(&acc_full[acc], acc_phase, a.status, a.timeout_ns)) break;
       ptx::tc_fence_after();
       const int64_t i = i0 + q * 32 + lane;
@@ -246,9 +321,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           out[e] = exp2_approx(d2 * a.scale);
         }
         if (TMA_STORE) {
-          if (lane == 0) ptx::bulk_wait_read<0>();  // previous store has read the buffer
+          // Two staging blocks per warp: the store issued two chunks ago has read this one.
+          uint8_t* blk = buf + (c & 1) * (32 * 32 * 4);
+          if (lane == 0) ptx::bulk_wait_read<1>();
           __syncwarp();
-          uint8_t* row = buf + lane * 128;
+          uint8_t* row = blk + lane * 128;
 #pragma unroll
           for (int c4 = 0; c4 < 8; ++c4) {
             *reinterpret_cast<float4*>(row + ((c4 ^ (lane & 7)) << 4)) =
@@ -257,7 +334,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           ptx::fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            ptx::tma_store_2d(&tm_k, buf, (int32_t)j, (int32_t)(i0 + q * 32));
+            ptx::tma_store_2d(&tm_k, blk, (int32_t)j, (int32_t)(i0 + q * 32));
             ptx::bulk_commit();
           }
         } else if (i < a.N) {
@@ -363,17 +440,21 @@ cudaError_t launch_forward_tc(const float* X, const float* Y, float* K, int64_t 
   const int64_t tiles = (int64_t)a.tiles_m * a.tiles_n;
   const int grid = (int)std::min<int64_t>(tiles, device_sm_count());
   cudaError_t e;
-  if (tma_store) {
-    e = cudaFuncSetAttribute(rbf_fwd_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    rbf_fwd_tc_kernel<true><<<grid, THREADS, SMEM_BYTES, stream>>>(txh, txl, tyh, tyl, tk, a);
-  } else {
-    e = cudaFuncSetAttribute(rbf_fwd_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    rbf_fwd_tc_kernel<false><<<grid, THREADS, SMEM_BYTES, stream>>>(txh, txl, tyh, tyl, tk, a);
-  }
+  const bool res_a = a.num_kc <= RA_CHUNKS;
+  auto launch = [&](auto kernel, size_t smem) -> cudaError_t {
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem);
+    if (err != cudaSuccess) return err;
+    kernel<<<grid, THREADS, smem, stream>>>(txh, txl, tyh, tyl, tk, a);
+    return cudaSuccess;
+  };
+  if (tma_store)
+    e = res_a ? launch(rbf_fwd_tc_kernel<true, true>, SMEM_BYTES_RA)
+              : launch(rbf_fwd_tc_kernel<true, false>, SMEM_BYTES);
+  else
+    e = res_a ? launch(rbf_fwd_tc_kernel<false, true>, SMEM_BYTES_RA)
+              : launch(rbf_fwd_tc_kernel<false, false>, SMEM_BYTES);
+  if (e != cudaSuccess) return e;
   note_launches(1);
   return cudaGetLastError();
 }

@@ -53,12 +53,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Wait for phase `parity` of `bar` to complete, for at most `timeout_ns` of wall time.  On
-// expiry it records RBF_ERR_TIMEOUT (7) in *status and returns false; the caller then winds
-// down instead of waiting forever.  Every wait of the persistent kernels goes through this.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status,
-                                                  uint64_t timeout_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
+// Slow path of mbar_wait_bounded, kept out of line so that the many wait sites of the
+// persistent kernels share one copy of the polling loop (instruction-cache footprint).
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* status,
+                                            uint64_t timeout_ns) {
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -67,6 +65,15 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
       return false;
     }
   }
+}
+
+// Wait for phase `parity` of `bar` to complete, for at most `timeout_ns` of wall time.  On
+// expiry it records RBF_ERR_TIMEOUT (7) in *status and returns false; the caller then winds
+// down instead of waiting forever.  Every wait of the persistent kernels goes through this.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status,
+                                                  uint64_t timeout_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, status, timeout_ns);
 }
 
 // ---------------------------------------------------------------- TMA (no multicast)
