@@ -16,10 +16,20 @@ namespace rbf {
 static std::atomic<uint64_t> g_launches{0};
 void note_launches(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* s = std::getenv("RBF_NO_PDL");
+    return !(s != nullptr && std::atoi(s) != 0);
+  }();
+  return on;
+}
+
 WaitConfig wait_config_from_env() {
   WaitConfig w;
   w.timeout_ns = 2000ull * 1000000ull;
   w.debug_skip_first_load = 0;
+  w.fwd_pair = 0;
+  if (const char* s = std::getenv("RBF_FWD_PAIR")) w.fwd_pair = std::atoi(s) != 0;
   if (const char* s = std::getenv("RBF_WAIT_TIMEOUT_MS")) {
     const long long ms = std::atoll(s);
     if (ms > 0) w.timeout_ns = (unsigned long long)ms * 1000000ull;

@@ -254,6 +254,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #ifdef RBF_TRACE
   if (threadIdx.x == 0 && blockIdx.x < 1024) g_cta_span[blockIdx.x][0] = ptx::globaltimer() & ((1ull << 48) - 1);
 #endif
+  ptx::griddep_wait();  // outputs zeroed and the workspace written by the previous kernels
 
   // Contiguous, balanced range of tiles for this CTA.
   const int64_t t_begin = a.total_tiles * blockIdx.x / gridDim.x;
@@ -595,6 +596,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) ptx::bulk_wait<0>();  // reduces complete before the CTA exits
   }
 
+  ptx::griddep_launch_dependents();
   ptx::tc_fence_before();
   __syncthreads();
 #ifdef RBF_TRACE
@@ -616,6 +618,8 @@ __global__ void __launch_bounds__(256) rbf_bwd_finalize_kernel(const float* __re
                                                                const float* __restrict__ rowsum,
                                                                float* __restrict__ dX, int64_t N,
                                                                int64_t D, float c) {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
   const int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // float4 index
   const int64_t per_row = D / 4;
   if (q >= N * per_row) return;
@@ -628,6 +632,21 @@ __global__ void __launch_bounds__(256) rbf_bwd_finalize_kernel(const float* __re
   v.z = fmaf(s, x.z, v.z);
   v.w = fmaf(s, x.w, v.w);
   reinterpret_cast<float4*>(dX)[q] = v;
+}
+
+// Zeroes the three accumulation targets of the backward (dX, dY, the rowsum vector) in one
+// launch, so the stream stays a chain of kernels that programmatic dependent launch can overlap.
+__global__ void __launch_bounds__(256) rbf_bwd_zero_kernel(float* __restrict__ a, int64_t na,
+                                                           float* __restrict__ b, int64_t nb,
+                                                           float* __restrict__ c, int64_t nc) {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < na + nb + nc; k += stride) {
+    if (k < na) a[k] = 0.f;
+    else if (k < na + nb) b[k - na] = 0.f;
+    else c[k - na - nb] = 0.f;
+  }
 }
 
 }  // namespace
@@ -646,14 +665,24 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
                                float* dX, float* dY, int64_t N, int64_t M, int64_t D,
                                float gamma, void* ws, const WaitConfig& wc, cudaStream_t stream) {
   cudaError_t e;
-  if (N * D > 0 && (e = cudaMemsetAsync(dX, 0, sizeof(float) * (size_t)(N * D), stream)) != cudaSuccess) return e;
-  if (M * D > 0 && (e = cudaMemsetAsync(dY, 0, sizeof(float) * (size_t)(M * D), stream)) != cudaSuccess) return e;
-  if (N == 0 || M == 0 || D == 0) return cudaSuccess;
   const PrepLayout L = prep_layout(N, M, D);
-  const int DS = (D <= 32) ? 32 : 64;
-  const int mn = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
   const bool tma_flush = (D % 4) == 0;  // dX rows 16-byte pitched
   float* rowsum = ws_at<float>(ws, L.end);
+  const bool work = N > 0 && M > 0 && D > 0;
+  {
+    const int64_t nr = (work && tma_flush) ? N : 0;
+    const int64_t total = N * D + M * D + nr;
+    if (total > 0) {
+      const int64_t blocks = std::min<int64_t>(ceil_div(total, 256), 4 * device_sm_count());
+      if ((e = launch_kernel(rbf_bwd_zero_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, dX,
+                             N * D, dY, M * D, rowsum, nr)) != cudaSuccess)
+        return e;
+      note_launches(1);
+    }
+  }
+  if (!work) return cudaGetLastError();
+  const int DS = (D <= 32) ? 32 : 64;
+  const int mn = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
   CUtensorMap tg, tk, txh, txl, tyh, tyl, tdx;
   if (!make_tmap_2d(&tg, G, N, M, M, 32, 128) || !make_tmap_2d(&tk, K, N, M, M, 32, 128) ||
       !make_tmap_2d(&txh, ws_at<float>(ws, L.xhi), N, L.Dp, L.Dp, 32, 32, mn) ||
@@ -663,7 +692,6 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
     return cudaErrorInvalidValue;
   if (tma_flush) {
     if (!make_tmap_2d(&tdx, dX, N, D, D, 32, 32)) return cudaErrorInvalidValue;
-    if ((e = cudaMemsetAsync(rowsum, 0, sizeof(float) * (size_t)N, stream)) != cudaSuccess) return e;
   } else {
     tdx = tg;  // unused
   }
@@ -694,21 +722,23 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
     if ((e = cudaFuncSetAttribute(rbf_bwd_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)Cfg<32>::SMEM)) != cudaSuccess)
       return e;
-    rbf_bwd_tc_kernel<32><<<grid, THREADS, Cfg<32>::SMEM, stream>>>(tg, tk, txh, txl, tyh, tyl,
-                                                                   tdx, a);
+    e = launch_kernel(rbf_bwd_tc_kernel<32>, dim3(grid), dim3(THREADS), Cfg<32>::SMEM, stream, tg,
+                      tk, txh, txl, tyh, tyl, tdx, a);
   } else {
     if ((e = cudaFuncSetAttribute(rbf_bwd_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)Cfg<64>::SMEM)) != cudaSuccess)
       return e;
-    rbf_bwd_tc_kernel<64><<<grid, THREADS, Cfg<64>::SMEM, stream>>>(tg, tk, txh, txl, tyh, tyl,
-                                                                   tdx, a);
+    e = launch_kernel(rbf_bwd_tc_kernel<64>, dim3(grid), dim3(THREADS), Cfg<64>::SMEM, stream, tg,
+                      tk, txh, txl, tyh, tyl, tdx, a);
   }
+  if (e != cudaSuccess) return e;
   note_launches(1);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if (tma_flush) {
     const int64_t n4 = N * (D / 4);
-    rbf_bwd_finalize_kernel<<<(unsigned)ceil_div(n4, 256), 256, 0, stream>>>(X, rowsum, dX, N, D,
-                                                                             a.c);
+    if ((e = launch_kernel(rbf_bwd_finalize_kernel, dim3((unsigned)ceil_div(n4, 256)), dim3(256), 0,
+                           stream, X, rowsum, dX, N, D, a.c)) != cudaSuccess)
+      return e;
     note_launches(1);
   }
   return cudaGetLastError();

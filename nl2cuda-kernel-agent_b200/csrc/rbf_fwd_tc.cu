@@ -37,20 +37,26 @@ namespace {
 constexpr int BM = 128;
 constexpr int BN = 128;
 constexpr int BK = 32;
-constexpr int STAGES = 2;
+constexpr int STAGES = 3;
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 32 * (2 + EPI_WARPS);
 constexpr uint32_t TILE_BYTES = 128 * BK * 4;  // 16 KiB: 128 rows x 128 bytes
 constexpr uint32_t STAGE_BYTES = 4 * TILE_BYTES;
-constexpr uint32_t EPI_BYTES = 2 * 32 * 32 * 4;  // two 32x32 fp32 staging blocks per warp
+constexpr int EPI_BUFS = 1;                                 // 32x32 fp32 staging blocks per warp
+constexpr uint32_t EPI_BYTES = EPI_BUFS * 32 * 32 * 4;
 constexpr uint32_t TMEM_COLS = 2 * BN;
 constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + EPI_WARPS * EPI_BYTES + 256;
 static_assert(SMEM_BYTES <= 232448, "forward shared memory over the sm_100 limit");
 // Resident-X variant (D <= 64, at most two 32-feature chunks): the CTA walks its tiles along j,
 // so the X hi/lo slices of one row block stay in shared memory and only Y is streamed.
 constexpr int RA_CHUNKS = 2;
-constexpr int RB_STAGES = 3;
+constexpr int RB_STAGES = 4;
 constexpr uint32_t CHUNK_BYTES = 2 * TILE_BYTES;  // hi + lo of one 32-feature slice, 128 rows
+// Pair variant (two-CTA clusters, tcgen05.mma.cta_group::2, M = 256): each CTA keeps its own 128
+// X rows resident and streams only 64 of the tile's 128 Y rows, so Y traffic per SM halves.
+constexpr int PB_STAGES = 8;
+constexpr uint32_t PCHUNK_BYTES = CHUNK_BYTES / 2;  // hi + lo of one slice, 64 rows
+constexpr int PAIR_ROWS = 64;
 constexpr size_t SMEM_BYTES_RA =
     1024 + (size_t)RA_CHUNKS * CHUNK_BYTES + RB_STAGES * CHUNK_BYTES + EPI_WARPS * EPI_BYTES + 256;
 static_assert(SMEM_BYTES_RA <= 232448, "forward shared memory over the sm_100 limit");
@@ -65,15 +71,23 @@ struct FwdArgs {
   int* status;
   unsigned long long timeout_ns;
   int debug_skip_first_load;
+  int ablate;  // development builds only (RBF_TRACE): 1 no MMA, 2 no epilogue math/store, 3 no store, 4 = 1+2
 };
 
-template <bool TMA_STORE, bool RES_A>
+#ifdef RBF_TRACE
+__device__ unsigned long long g_fwd_span[1024][3];
+#endif
+
+template <bool TMA_STORE, bool RES_A, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     rbf_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_xhi,
                       const __grid_constant__ CUtensorMap tm_xlo,
                       const __grid_constant__ CUtensorMap tm_yhi,
                       const __grid_constant__ CUtensorMap tm_ylo,
                       const __grid_constant__ CUtensorMap tm_k, const FwdArgs a) {
+#ifdef RBF_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 1024) g_fwd_span[blockIdx.x][2] = ptx::globaltimer();
+#endif
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -82,19 +96,23 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* stage_mem = smem;
   uint8_t* epi_mem = smem + (RES_A ? (RA_CHUNKS + RB_STAGES) * CHUNK_BYTES : STAGES * STAGE_BYTES);
   uint64_t* bars = reinterpret_cast<uint64_t*>(epi_mem + EPI_WARPS * EPI_BYTES);
-  uint64_t* full = bars;                  // [4]  TMA -> MMA (operand stage)
-  uint64_t* empty = bars + 4;             // [4]  MMA -> TMA
-  uint64_t* a_full = bars + 8;            // resident X landed   TMA -> MMA
-  uint64_t* a_empty = bars + 9;           // resident X released MMA -> TMA
-  uint64_t* acc_full = bars + 10;         // [2]       MMA -> epilogue
+  uint64_t* full = bars;                  // [8]  TMA -> MMA (operand stage)
+  uint64_t* empty = bars + 8;             // [8]  MMA -> TMA
+  uint64_t* a_full = bars + 16;           // resident X landed   TMA -> MMA
+  uint64_t* a_empty = bars + 17;          // resident X released MMA -> TMA
+  uint64_t* acc_full = bars + 18;         // [2]       MMA -> epilogue
   uint64_t* acc_empty = acc_full + 2;     // [2]       epilogue -> MMA
   uint64_t* drain = acc_empty + 2;        // [1]       MMA teardown
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // Pair variant: rank 0 of the cluster issues the MMAs and owns the barriers that count both
+  // CTAs' operand bytes (full, a_full) and both CTAs' epilogue releases (acc_empty).
+  const uint32_t rank = PAIR ? ptx::cluster_ctarank() : 0;
+  const bool leader = rank == 0;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < 4; ++s) {
+    for (int s = 0; s < 8; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 1);
     }
@@ -102,7 +120,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     ptx::mbar_init(a_empty, 1);
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(&acc_full[b], 1);
-      ptx::mbar_init(&acc_empty[b], EPI_WARPS);
+      ptx::mbar_init(&acc_empty[b], PAIR ? 2 * EPI_WARPS : EPI_WARPS);
     }
     ptx::mbar_init(drain, 1);
     ptx::fence_mbar_init();
@@ -114,23 +132,41 @@ __global__ void __launch_bounds__(THREADS, 1)
     ptx::prefetch_tensormap(&tm_ylo);
     if (TMA_STORE) ptx::prefetch_tensormap(&tm_k);
   }
+  if (PAIR) ptx::cluster_sync();  // the peer's barriers exist before any remote arrive
   if (warp == 1) {
-    ptx::tmem_alloc(tmem_slot, TMEM_COLS);
-    ptx::tmem_relinquish();
+    if (PAIR) {
+      ptx::tmem_alloc_pair(tmem_slot, TMEM_COLS);
+      ptx::tmem_relinquish_pair();
+    } else {
+      ptx::tmem_alloc(tmem_slot, TMEM_COLS);
+      ptx::tmem_relinquish();
+    }
   }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+#ifdef RBF_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 1024) g_fwd_span[blockIdx.x][0] = ptx::globaltimer();
+#endif
+  ptx::griddep_wait();  // the split pass (previous kernel) has written the workspace
   // Contiguous, balanced tile range per CTA; tiles run along j (t -> ib = t / tiles_n).
+  // Pair variant: the unit is the cluster and a tile is 256 rows (128 per CTA) x 128 columns.
   const int64_t num_tiles = (int64_t)a.tiles_m * a.tiles_n;
-  const int64_t t_begin = num_tiles * blockIdx.x / gridDim.x;
-  const int64_t t_end = num_tiles * (blockIdx.x + 1) / gridDim.x;
+  const int64_t unit = PAIR ? (blockIdx.x >> 1) : blockIdx.x;
+  const int64_t units = PAIR ? (gridDim.x >> 1) : gridDim.x;
+  const int64_t t_begin = num_tiles * unit / units;
+  const int64_t t_end = num_tiles * (unit + 1) / units;
+  constexpr int TILE_ROWS = PAIR ? 2 * BM : BM;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0 && RES_A) {
-      constexpr int NS = RB_STAGES;
+      constexpr int NS = PAIR ? PB_STAGES : RB_STAGES;
+      constexpr uint32_t BSTAGE = PAIR ? PCHUNK_BYTES : CHUNK_BYTES;
+      constexpr uint32_t PEERS = PAIR ? 2 : 1;
+      uint8_t* bring = stage_mem + RA_CHUNKS * CHUNK_BYTES;
+      const uint32_t a_full_c = PAIR ? ptx::map_to_rank(a_full, 0) : 0;
       int stage = 0;
       uint32_t phase = 0, a_phase = 0;
       int last_parity[NS], a_issued = -1;
@@ -139,17 +175,23 @@ __global__ void __launch_bounds__(THREADS, 1)
       int cur_ib = -1;
       for (int64_t t = t_begin; t < t_end && ok; ++t) {
         const int ib = (int)(t / a.tiles_n);
-        const int i0 = ib * BM, j0 = (int)(t % a.tiles_n) * BN;
+        const int i0 = ib * TILE_ROWS + (int)rank * BM;
+        const int j0 = (int)(t % a.tiles_n) * BN + (PAIR ? (int)rank * PAIR_ROWS : 0);
         if (ib != cur_ib) {
           cur_ib = ib;
           if (!ptx::mbar_wait_bounded(a_empty, a_phase ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
-          ptx::mbar_arrive_expect_tx(a_full, (uint32_t)a.num_kc * CHUNK_BYTES);
+          if (leader) ptx::mbar_arrive_expect_tx(a_full, PEERS * (uint32_t)a.num_kc * CHUNK_BYTES);
           for (int kc = 0; kc < a.num_kc; ++kc) {
             uint8_t* am = stage_mem + kc * CHUNK_BYTES;
-            ptx::tma_load_2d(am, &tm_xhi, kc * BK, i0, a_full);
-            ptx::tma_load_2d(am + TILE_BYTES, &tm_xlo, kc * BK, i0, a_full);
+            if (PAIR) {
+              ptx::tma_load_2d_pair(am, &tm_xhi, kc * BK, i0, a_full_c);
+              ptx::tma_load_2d_pair(am + TILE_BYTES, &tm_xlo, kc * BK, i0, a_full_c);
+            } else {
+              ptx::tma_load_2d(am, &tm_xhi, kc * BK, i0, a_full);
+              ptx::tma_load_2d(am + TILE_BYTES, &tm_xlo, kc * BK, i0, a_full);
+            }
           }
-          a_issued = (int)a_phase;
+          if (leader) a_issued = (int)a_phase;
           a_phase ^= 1;
         }
         for (int kc = 0; kc < a.num_kc; ++kc) {
@@ -157,16 +199,24 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (a.debug_skip_first_load && !skipped && blockIdx.x == 0) {
             skipped = true;  // test hook: this stage never fills, so its consumer times out
           } else {
-            uint8_t* bm = stage_mem + (RA_CHUNKS + stage) * CHUNK_BYTES;
-            ptx::mbar_arrive_expect_tx(&full[stage], CHUNK_BYTES);
-            ptx::tma_load_2d(bm, &tm_yhi, kc * BK, j0, &full[stage]);
-            ptx::tma_load_2d(bm + TILE_BYTES, &tm_ylo, kc * BK, j0, &full[stage]);
-            last_parity[stage] = (int)phase;
+            uint8_t* bm = bring + stage * BSTAGE;
+            if (leader) ptx::mbar_arrive_expect_tx(&full[stage], PEERS * BSTAGE);
+            if (PAIR) {
+              const uint32_t fc = ptx::map_to_rank(&full[stage], 0);
+              ptx::tma_load_2d_pair(bm, &tm_yhi, kc * BK, j0, fc);
+              ptx::tma_load_2d_pair(bm + BSTAGE / 2, &tm_ylo, kc * BK, j0, fc);
+            } else {
+              ptx::tma_load_2d(bm, &tm_yhi, kc * BK, j0, &full[stage]);
+              ptx::tma_load_2d(bm + BSTAGE / 2, &tm_ylo, kc * BK, j0, &full[stage]);
+            }
+            if (leader) last_parity[stage] = (int)phase;
           }
           if (++stage == NS) { stage = 0; phase ^= 1; }
         }
       }
-      if (!ok) {  // let every load this thread issued land before the CTA exits
+      // Let every load issued land before the CTA exits (in the pair variant the leader's
+      // barriers count both CTAs' bytes, and the final cluster barrier holds the peer until then).
+      if (!ok) {
         for (int s = 0; s < NS; ++s)
           if (last_parity[s] >= 0)
             ptx::mbar_wait_bounded(&full[s], (uint32_t)last_parity[s], a.status, a.timeout_ns);
@@ -213,9 +263,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = ptx::idesc_tf32(BM, BN, 0, 0);
-      constexpr int NS = RES_A ? RB_STAGES : STAGES;
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = ptx::idesc_tf32(PAIR ? 2 * BM : BM, BN, 0, 0);
+      constexpr int NS = PAIR ? PB_STAGES : (RES_A ? RB_STAGES : STAGES);
+      constexpr uint32_t BSTAGE = PAIR ? PCHUNK_BYTES : CHUNK_BYTES;
+      // Pair variant: the commit arrives on the same barrier in both CTAs.
+      auto commit = [](uint64_t* bar) {
+        if (PAIR) ptx::mma_commit_pair(bar);
+        else ptx::mma_commit(bar);
+      };
       int stage = 0;
       uint32_t phase = 0, a_phase = 0;
       int acc = 0;
@@ -244,36 +300,47 @@ __global__ void __launch_bounds__(THREADS, 1)
           // Operand bases: A = X hi|lo, B = Y hi|lo of this K chunk.
           const uint32_t abase = RES_A ? ptx::smem_u32(stage_mem + kc * CHUNK_BYTES)
                                        : ptx::smem_u32(stage_mem + stage * STAGE_BYTES);
-          const uint32_t bbase = RES_A ? ptx::smem_u32(stage_mem + (RA_CHUNKS + stage) * CHUNK_BYTES)
-                                       : abase + 2 * TILE_BYTES;
+          const uint32_t bbase =
+              RES_A ? ptx::smem_u32(stage_mem + RA_CHUNKS * CHUNK_BYTES + stage * BSTAGE)
+                    : abase + 2 * TILE_BYTES;
+          const uint32_t blo_off = RES_A ? BSTAGE / 2 : TILE_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 8; ++k) {
             const uint32_t off = (uint32_t)k * 32;  // 8 tf32 = 32 bytes along the swizzled row
             const uint64_t ahi = ptx::smem_desc(abase + off, 16, 1024, 2);
             const uint64_t alo = ptx::smem_desc(abase + TILE_BYTES + off, 16, 1024, 2);
             const uint64_t bhi = ptx::smem_desc(bbase + off, 16, 1024, 2);
-            const uint64_t blo = ptx::smem_desc(bbase + TILE_BYTES + off, 16, 1024, 2);
-            ptx::mma_tf32_ss(d, ahi, bhi, idesc, (kc | k) != 0);
-            ptx::mma_tf32_ss(d, ahi, blo, idesc, 1);
-            ptx::mma_tf32_ss(d, alo, bhi, idesc, 1);
+            const uint64_t blo = ptx::smem_desc(bbase + blo_off + off, 16, 1024, 2);
+#ifdef RBF_TRACE
+            if (a.ablate == 1 || a.ablate == 4) continue;
+#endif
+            if (PAIR) {
+              ptx::mma_tf32_ss_pair(d, ahi, bhi, idesc, (kc | k) != 0);
+              ptx::mma_tf32_ss_pair(d, ahi, blo, idesc, 1);
+              ptx::mma_tf32_ss_pair(d, alo, bhi, idesc, 1);
+            } else {
+              ptx::mma_tf32_ss(d, ahi, bhi, idesc, (kc | k) != 0);
+              ptx::mma_tf32_ss(d, ahi, blo, idesc, 1);
+              ptx::mma_tf32_ss(d, alo, bhi, idesc, 1);
+            }
           }
-          ptx::mma_commit(&empty[stage]);
+          commit(&empty[stage]);
           if (++stage == NS) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        ptx::mma_commit(&acc_full[acc]);
+        commit(&acc_full[acc]);
         // Last tile of this row block: the resident X may be replaced once these MMAs finish.
-        if (RES_A && (t + 1 == t_end || (int)((t + 1) / a.tiles_n) != ib)) ptx::mma_commit(a_empty);
+        if (RES_A && (t + 1 == t_end || (int)((t + 1) / a.tiles_n) != ib)) commit(a_empty);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;
         }
       }
       // Teardown: every MMA issued so far must finish before TMEM is freed.
-      ptx::mma_commit(drain);
+      commit(drain);
       ptx::mbar_wait_bounded(drain, 0, a.status, a.timeout_ns);
     }
   } else {
@@ -283,47 +350,76 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t* buf = epi_mem + (warp - 2) * EPI_BYTES;
     int acc = 0;
     uint32_t acc_phase = 0;
+    // The norms of the next chunk are loaded one chunk ahead (and across tiles), so their
+    // global-load latency overlaps the accumulator wait and the previous chunk's math.
+    auto load_yn = [&](int64_t t, int c, float (&dst)[32]) {
+      const int64_t j = (t % a.tiles_n) * BN + h * 64 + c * 32;
+      if (j + 32 <= a.M) {
+        const float4* y4 = reinterpret_cast<const float4*>(a.yn + j);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float4 f = __ldg(y4 + e);
+          dst[4 * e] = f.x; dst[4 * e + 1] = f.y; dst[4 * e + 2] = f.z; dst[4 * e + 3] = f.w;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) dst[e] = (j + e < a.M) ? __ldg(a.yn + j + e) : 0.f;
+      }
+    };
+    auto load_xn = [&](int64_t t) {
+      const int64_t i = (t / a.tiles_n) * TILE_ROWS + rank * BM + q * 32 + lane;
+      return i < a.N ? __ldg(a.xn + i) : 0.f;
+    };
+    float ynext[32];
+    float xnext = 0.f;
+    if (t_begin < t_end) {
+      load_yn(t_begin, 0, ynext);
+      xnext = load_xn(t_begin);
+    }
     for (int64_t t = t_begin; t < t_end; ++t) {
-      const int64_t i0 = (t / a.tiles_n) * BM;
+      const int64_t i0 = (t / a.tiles_n) * TILE_ROWS + rank * BM;
       const int64_t j0 = (t % a.tiles_n) * BN;
       if (!ptx::mbar_wait_bounded(&acc_full[acc], acc_phase, a.status, a.timeout_ns)) break;
       ptx::tc_fence_after();
       const int64_t i = i0 + q * 32 + lane;
-      const float xi = i < a.N ? __ldg(a.xn + i) : 0.f;
-#pragma unroll 1
+      const float xi = xnext;
+      if (t + 1 < t_end) xnext = load_xn(t + 1);
+#pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int col0 = h * 64 + c * 32;
+        float yv[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) yv[e] = ynext[e];
+        if (c == 0) load_yn(t, 1, ynext);
+        else if (t + 1 < t_end) load_yn(t + 1, 0, ynext);
         uint32_t v[32];
         ptx::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + col0), v);
         ptx::tmem_wait_ld();
         if (c == 1) {
           ptx::tc_fence_before();
           __syncwarp();
-          if (lane == 0) ptx::mbar_arrive(&acc_empty[acc]);
+          if (lane == 0) {
+            if (PAIR) ptx::mbar_arrive_cluster(ptx::map_to_rank(&acc_empty[acc], 0));
+            else ptx::mbar_arrive(&acc_empty[acc]);
+          }
         }
         const int64_t j = j0 + col0;
-        float yv[32];
-        if (j + 32 <= a.M) {
-          const float4* y4 = reinterpret_cast<const float4*>(a.yn + j);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float4 f = __ldg(y4 + e);
-            yv[4 * e] = f.x; yv[4 * e + 1] = f.y; yv[4 * e + 2] = f.z; yv[4 * e + 3] = f.w;
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) yv[e] = (j + e < a.M) ? __ldg(a.yn + j + e) : 0.f;
-        }
+#ifdef RBF_TRACE
+        if (a.ablate == 2 || a.ablate == 4) continue;
+#endif
         float out[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const float d2 = fmaxf(fmaf(-2.f, __uint_as_float(v[e]), xi + yv[e]), 0.f);
           out[e] = exp2_approx(d2 * a.scale);
         }
+#ifdef RBF_TRACE
+        if (a.ablate == 3) { if (out[lane] == 12345.f) a.K[0] = 1.f; continue; }
+#endif
         if (TMA_STORE) {
-          // Two staging blocks per warp: the store issued two chunks ago has read this one.
-          uint8_t* blk = buf + (c & 1) * (32 * 32 * 4);
-          if (lane == 0) ptx::bulk_wait_read<1>();
+          // EPI_BUFS staging blocks per warp, reused once the store that last read them is done.
+          uint8_t* blk = buf + (c % EPI_BUFS) * (32 * 32 * 4);
+          if (lane == 0) ptx::bulk_wait_read<EPI_BUFS - 1>();
           __syncwarp();
           uint8_t* row = blk + lane * 128;
 #pragma unroll
@@ -352,11 +448,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (TMA_STORE && lane == 0) ptx::bulk_wait<0>();
   }
 
+  ptx::griddep_launch_dependents();
   ptx::tc_fence_before();
   __syncthreads();
+  // Pair variant: the leader's MMAs read the peer's shared memory and write its TMEM, and the
+  // peer arrives on the leader's barriers; neither CTA leaves (or frees TMEM) before both are done.
+  if (PAIR) ptx::cluster_sync();
+#ifdef RBF_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 1024) g_fwd_span[blockIdx.x][1] = ptx::globaltimer();
+#endif
   if (warp == 1) {
     ptx::tc_fence_after();
-    ptx::tmem_dealloc(tmem, TMEM_COLS);
+    if (PAIR) ptx::tmem_dealloc_pair(tmem, TMEM_COLS);
+    else ptx::tmem_dealloc(tmem, TMEM_COLS);
   }
 }
 
@@ -406,6 +510,44 @@ int device_sm_count() {
   return n > 0 ? n : kSmCount;
 }
 
+// How many two-CTA clusters of the pair forward fit on the device at once (0 = do not use the
+// pair variant: fewer than half the SMs could take part).  Cached per device.
+static cudaError_t pair_capacity(int* clusters) {
+  static int cached[64];
+  static bool known[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 64 && known[dev]) {
+    *clusters = cached[dev];
+    return cudaSuccess;
+  }
+  auto kernel = rbf_fwd_tc_kernel<true, true, true>;
+  if ((e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)SMEM_BYTES_RA)) != cudaSuccess)
+    return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * (unsigned)device_sm_count());
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = SMEM_BYTES_RA;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if ((e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg)) != cudaSuccess) return e;
+  if (2 * n < device_sm_count() / 2) n = 0;
+  if (dev < 64) {
+    cached[dev] = n;
+    known[dev] = true;
+  }
+  *clusters = n;
+  return cudaSuccess;
+}
+
 cudaError_t launch_forward_tc(const float* X, const float* Y, float* K, int64_t N, int64_t M,
                               int64_t D, float gamma, void* ws, const WaitConfig& wc,
                               cudaStream_t stream) {
@@ -437,26 +579,61 @@ cudaError_t launch_forward_tc(const float* X, const float* Y, float* K, int64_t 
   a.status = ws_at<int>(ws, L.status);
   a.timeout_ns = wc.timeout_ns;
   a.debug_skip_first_load = wc.debug_skip_first_load;
-  const int64_t tiles = (int64_t)a.tiles_m * a.tiles_n;
-  const int grid = (int)std::min<int64_t>(tiles, device_sm_count());
+  a.ablate = 0;
+#ifdef RBF_TRACE
+  if (const char* ab = std::getenv("RBF_ABLATE")) a.ablate = std::atoi(ab);
+#endif
   cudaError_t e;
   const bool res_a = a.num_kc <= RA_CHUNKS;
-  auto launch = [&](auto kernel, size_t smem) -> cudaError_t {
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)smem);
-    if (err != cudaSuccess) return err;
-    kernel<<<grid, THREADS, smem, stream>>>(txh, txl, tyh, tyl, tk, a);
-    return cudaSuccess;
-  };
-  if (tma_store)
-    e = res_a ? launch(rbf_fwd_tc_kernel<true, true>, SMEM_BYTES_RA)
-              : launch(rbf_fwd_tc_kernel<true, false>, SMEM_BYTES);
-  else
-    e = res_a ? launch(rbf_fwd_tc_kernel<false, true>, SMEM_BYTES_RA)
-              : launch(rbf_fwd_tc_kernel<false, false>, SMEM_BYTES);
+  // Pair variant: D <= 64, TMA-stored K, and enough two-CTA clusters resident at once.
+  int pair_clusters = 0;
+  if (res_a && tma_store && wc.fwd_pair) {
+    if ((e = pair_capacity(&pair_clusters)) != cudaSuccess) return e;
+  }
+  if (pair_clusters > 0) {
+    CUtensorMap tyh2, tyl2;  // 64-row Y boxes: each CTA of the pair loads half of a Y tile
+    if (!make_tmap_2d(&tyh2, ws_at<float>(ws, L.yhi), M, L.Dp, L.Dp, BK, PAIR_ROWS) ||
+        !make_tmap_2d(&tyl2, ws_at<float>(ws, L.ylo), M, L.Dp, L.Dp, BK, PAIR_ROWS))
+      return cudaErrorInvalidValue;
+    a.tiles_m = (int)ceil_div(N, 2 * BM);
+    const int64_t tiles = (int64_t)a.tiles_m * a.tiles_n;
+    const int clusters = (int)std::min<int64_t>(tiles, pair_clusters);
+    auto kernel = rbf_fwd_tc_kernel<true, true, true>;
+    if ((e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)SMEM_BYTES_RA)) != cudaSuccess)
+      return e;
+    e = launch_kernel_cluster(kernel, dim3(2 * clusters), dim3(THREADS), SMEM_BYTES_RA, 2, stream,
+                              txh, txl, tyh2, tyl2, tk, a);
+  } else {
+    const int64_t tiles = (int64_t)a.tiles_m * a.tiles_n;
+    const int grid = (int)std::min<int64_t>(tiles, device_sm_count());
+    auto launch = [&](auto kernel, size_t smem) -> cudaError_t {
+      cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+      if (err != cudaSuccess) return err;
+      return launch_kernel(kernel, dim3(grid), dim3(THREADS), smem, stream, txh, txl, tyh, tyl,
+                           tk, a);
+    };
+    if (tma_store)
+      e = res_a ? launch(rbf_fwd_tc_kernel<true, true, false>, SMEM_BYTES_RA)
+                : launch(rbf_fwd_tc_kernel<true, false, false>, SMEM_BYTES);
+    else
+      e = res_a ? launch(rbf_fwd_tc_kernel<false, true, false>, SMEM_BYTES_RA)
+                : launch(rbf_fwd_tc_kernel<false, false, false>, SMEM_BYTES);
+  }
   if (e != cudaSuccess) return e;
   note_launches(1);
   return cudaGetLastError();
 }
 
 }  // namespace rbf
+
+#ifdef RBF_TRACE
+extern "C" __attribute__((visibility("default"))) int rbf_debug_fwd_spans(unsigned long long* out) {
+  return (int)cudaMemcpyFromSymbol(out, rbf::g_fwd_span, sizeof(rbf::g_fwd_span));
+}
+extern "C" __attribute__((visibility("default"))) int rbf_debug_fwd_spans_clear() {
+  static unsigned long long z[1024][3];
+  return (int)cudaMemcpyToSymbol(rbf::g_fwd_span, z, sizeof(z));
+}
+#endif

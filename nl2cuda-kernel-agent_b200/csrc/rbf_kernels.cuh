@@ -5,7 +5,52 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace rbf {
+
+// Programmatic dependent launch of the library's kernels (on unless RBF_NO_PDL=1): each launch
+// carries cudaLaunchAttributeProgrammaticStreamSerialization, so its prologue may overlap the
+// tail of the previous kernel in the stream; the kernels wait (griddepcontrol.wait) before
+// touching global memory, so stream order is kept for every byte they read or write.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Same, launched as clusters of `cluster_x` CTAs along x (gridDim.x a multiple of it).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                  unsigned cluster_x, cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster_x;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Bound of every device-side mbarrier wait, and the test hook that makes one wait run out.
 // Read from the environment at each call: RBF_WAIT_TIMEOUT_MS (default 2000) and
@@ -14,6 +59,7 @@ namespace rbf {
 struct WaitConfig {
   unsigned long long timeout_ns;
   int debug_skip_first_load;
+  int fwd_pair;  // RBF_FWD_PAIR (default 0): 1 runs the D <= 64 forward on two-CTA clusters
 };
 WaitConfig wait_config_from_env();
 

@@ -9,6 +9,7 @@
 // and (N+M)*(2*Dp+1)*4 out.
 #include "rbf_common.cuh"
 #include "rbf_kernels.cuh"
+#include "rbf_ptx.cuh"
 
 namespace rbf {
 
@@ -17,6 +18,8 @@ __global__ void __launch_bounds__(256) prep_split_kernel(
     int64_t Dp, float* __restrict__ xn, float* __restrict__ yn, float* __restrict__ xhi,
     float* __restrict__ xlo, float* __restrict__ yhi, float* __restrict__ ylo,
     int* __restrict__ status) {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
   if (blockIdx.x == 0 && threadIdx.x == 0) *status = RBF_OK;  // fresh workspace: no error yet
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -47,10 +50,12 @@ cudaError_t launch_prep(const float* X, const float* Y, int64_t N, int64_t M, in
   if (rows == 0) return cudaSuccess;
   const int warps_per_block = 8;
   const int64_t blocks = ceil_div(rows, warps_per_block);
-  prep_split_kernel<<<(unsigned)blocks, 32 * warps_per_block, 0, stream>>>(
-      X, Y, N, M, D, L.Dp, ws_at<float>(ws, L.xn), ws_at<float>(ws, L.yn),
-      ws_at<float>(ws, L.xhi), ws_at<float>(ws, L.xlo), ws_at<float>(ws, L.yhi),
-      ws_at<float>(ws, L.ylo), ws_at<int>(ws, L.status));
+  const cudaError_t e = launch_kernel(
+      prep_split_kernel, dim3((unsigned)blocks), dim3(32 * warps_per_block), 0, stream, X, Y, N,
+      M, D, L.Dp, ws_at<float>(ws, L.xn), ws_at<float>(ws, L.yn), ws_at<float>(ws, L.xhi),
+      ws_at<float>(ws, L.xlo), ws_at<float>(ws, L.yhi), ws_at<float>(ws, L.ylo),
+      ws_at<int>(ws, L.status));
+  if (e != cudaSuccess) return e;
   note_launches(1);
   return cudaGetLastError();
 }

@@ -127,3 +127,28 @@ def test_empty_sizes(cuda_device):
         if N and M:
             assert torch.all(K == 1.0)  # D = 0: distance 0
         assert torch.all(dX == 0) and torch.all(dY == 0)
+
+
+PAIR_SHAPES = [(1, 4, 1, 0.5), (129, 260, 32, 0.5 / 32), (257, 128, 64, 1 / 64),
+               (300, 516, 48, 0.02), (513, 1028, 64, 1 / 64), (4096, 4096, 64, 1 / 64)]
+
+
+@pytest.mark.parametrize("N,M,D,gamma", PAIR_SHAPES)
+def test_forward_pair_and_single_cta_variants(N, M, D, gamma, cuda_device, monkeypatch):
+    """D <= 64 with M % 4 == 0: RBF_FWD_PAIR=1 runs the two-CTA (cta_group::2) forward, 0 (the
+    default) single-CTA tiles.  Both must meet the gate against the oracle."""
+    from cases.rbf import native
+    r = np.random.default_rng(N + 7 * M + 13 * D)
+    X = r.standard_normal((N, D)).astype(np.float32)
+    Y = r.standard_normal((M, D)).astype(np.float32)
+    Xd, Yd = to_dev(X, Y)
+    rows = np.unique(np.linspace(0, N - 1, min(N, 256)).astype(np.int64))
+    Kr = oracle.forward(X[rows], Y, gamma)
+    out = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("RBF_FWD_PAIR", flag)
+        K = native.rbf_forward(Xd, Yd, gamma)
+        torch.cuda.synchronize()
+        out[flag] = K.cpu().numpy()
+        assert_gate(f"K pair={flag}", out[flag][rows], Kr)
+    np.testing.assert_allclose(out["1"], out["0"], rtol=1e-5, atol=1e-6)
