@@ -19,9 +19,14 @@
 // 32-byte-atom layout (descriptor layout type 1, TMA CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B): the
 // only shared-memory layout the tensor core accepts for MN-major tf32.
 //
-// Work split: tiles are ordered (feature slice, j-block, i-block) and every CTA takes a
-// contiguous range, so within a j-block "segment" the dY accumulator stays in TMEM across all
-// its i-blocks and is flushed at the segment end (red.add of c*(colsum*y - acc)).  The dX
+// Work split: tiles are ordered (feature slice, j-group, i-block, j-block within the group) and
+// the CTAs are split into `group` interleaved sub-grids, one per j-block of a group, so
+// neighbouring CTAs read neighbouring column blocks of the same rows at the same time.  Each CTA
+// first walks a contiguous static range of i-blocks of one j-block -- a "segment", over which
+// the dY accumulator stays in TMEM and is flushed once at the end (red.add of
+// c*(colsum*y - acc)) -- then claims tail tiles one at a time from a global counter, so CTAs
+// that run fast take more of the tail.  The strip producer decides the sequence and hands it to
+// the other roles through a 4-entry ring in shared memory.  The dX
 // accumulator is flushed once per tile: -c*acc is staged in shared memory and added into dX by
 // a TMA reduce-add, rowsum is added into a per-row vector, and a finalize pass adds
 // c*rowsum*x once per row.  The outputs are zeroed first; the fp32 summation order of dX / dY
@@ -84,7 +89,11 @@ struct BwdArgs {
   unsigned long long timeout_ns;
   int debug_skip_first_load;
   int tma_flush;  // dX partials are added by TMA reduce (needs D % 4 == 0)
-  int ablate;     // development builds only (RBF_TRACE): 1 skip dX reduce, 2 skip rowsum add
+  int group;             // neighbouring j-blocks walked together (divides tiles_j and the grid)
+  int64_t static_rows;   // group rows [0, static_rows) are split into contiguous per-CTA ranges;
+  int* counter;          // tiles from static_rows * group on are claimed from this counter
+  int ablate;     // development builds only (RBF_TRACE): 1 skip dX reduce, 2 skip rowsum add,
+                  // 4 C-warps skip W^T, 8 R-warps skip W, 16 no MMAs, 32 skip dY flush
 };
 
 struct TileCoord {
@@ -110,12 +119,27 @@ __device__ __forceinline__ void trace(int role, int code) {
 #define TRACE(role, code) ((void)0)
 #endif
 
-__device__ __forceinline__ TileCoord tile_of(int64_t t, const BwdArgs& a) {
+// Tile index u -> (feature slice, j-block, i-block).  Order: jsub (the j-block within a group
+// of `group` neighbours) fastest, then i-block, then j-group, then slice.  CTAs b with the same
+// b / group walk the same i-blocks of `group` neighbouring j-blocks at the same time, so the
+// row segments of G and K they read are contiguous over group x 512 bytes in DRAM.
+__device__ __forceinline__ TileCoord tile_of(int64_t u, const BwdArgs& a) {
   TileCoord c;
-  c.ib = (int)(t % a.tiles_i);
-  const int64_t r = t / a.tiles_i;
-  c.jb = (int)(r % a.tiles_j);
-  c.slice = (int)(r / a.tiles_j);
+#ifdef RBF_TRACE
+  if (a.ablate & 128) {  // row-raster order: j-blocks fastest
+    c.jb = (int)(u % a.tiles_j);
+    c.ib = (int)((u / a.tiles_j) % a.tiles_i);
+    c.slice = (int)(u / ((int64_t)a.tiles_j * a.tiles_i));
+    return c;
+  }
+#endif
+  const int jsub = (int)(u % a.group);
+  const int64_t r = u / a.group;
+  c.ib = (int)(r % a.tiles_i);
+  const int64_t r2 = r / a.tiles_i;
+  const int jgroups = a.tiles_j / a.group;
+  c.jb = (int)(r2 % jgroups) * a.group + jsub;
+  c.slice = (int)(r2 / jgroups);
   return c;
 }
 
@@ -123,9 +147,32 @@ __device__ __forceinline__ bool same_segment(const TileCoord& p, const TileCoord
   return p.slice == q.slice && p.jb == q.jb;
 }
 
-__device__ __forceinline__ bool segment_ends(int64_t t, int64_t t_end, const TileCoord& tc,
-                                             const BwdArgs& a) {
-  return t + 1 == t_end || !same_segment(tile_of(t + 1, a), tc);
+// The CTA's tile sequence (its static range, then tiles claimed from the global counter) is
+// decided by the strip producer and handed to every other role through a small ring in shared
+// memory: entry = tile index (-1 = no more work) + whether the dY segment ends with that tile.
+constexpr int SQ = 4;
+constexpr int SQ_CONSUMERS = 11;  // warps 1..11
+struct SchedRing {
+  volatile long long* tile;
+  volatile int* seg_end;
+  uint64_t* full;
+  uint64_t* empty;
+  int slot;
+  uint32_t ph;
+};
+
+__device__ __forceinline__ bool sched_pop(SchedRing& r, bool whole_warp, const BwdArgs& a,
+                                          int64_t& t, bool& seg_end) {
+  if (!ptx::mbar_wait_bounded(&r.full[r.slot], r.ph, a.status, a.timeout_ns)) return false;
+  t = r.tile[r.slot];
+  seg_end = r.seg_end[r.slot] != 0;
+  if (whole_warp) __syncwarp();
+  if (!whole_warp || (threadIdx.x & 31) == 0) ptx::mbar_arrive(&r.empty[r.slot]);
+  if (++r.slot == SQ) {
+    r.slot = 0;
+    r.ph ^= 1;
+  }
+  return true;
 }
 
 __device__ __forceinline__ void red_add4(float* p, float a, float b, float c, float d) {
@@ -206,7 +253,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* dy_full = dx_empty + 1;  // dY accumulator complete     dY issuer -> C-warps
   uint64_t* dy_empty = dy_full + 1;  // dY accumulator drained      C-warps -> dY issuer
   uint64_t* drain = dy_empty + 1;    // teardown of both issuers
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* sq_full = drain + 1;     // [SQ] tile entry written   producer -> every role
+  uint64_t* sq_empty = sq_full + SQ; // [SQ] tile entry read      every role -> producer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sq_empty + SQ);
+  long long* sq_tile = reinterpret_cast<long long*>(sq_empty + SQ + 1);
+  int* sq_seg_end = reinterpret_cast<int*>(sq_tile + SQ);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -230,6 +281,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     ptx::mbar_init(dy_full, 1);
     ptx::mbar_init(dy_empty, 4);
     ptx::mbar_init(drain, 2);  // one commit per MMA issuer
+    for (int s = 0; s < SQ; ++s) {
+      ptx::mbar_init(&sq_full[s], 1);
+      ptx::mbar_init(&sq_empty[s], SQ_CONSUMERS);
+    }
     ptx::fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -256,9 +311,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #endif
   ptx::griddep_wait();  // outputs zeroed and the workspace written by the previous kernels
 
-  // Contiguous, balanced range of tiles for this CTA.
-  const int64_t t_begin = a.total_tiles * blockIdx.x / gridDim.x;
-  const int64_t t_end = a.total_tiles * (blockIdx.x + 1) / gridDim.x;
+  SchedRing sq = {sq_tile, sq_seg_end, sq_full, sq_empty, 0, 0};
 
   if (warp == 0) {
     if (lane == 0) {
@@ -270,8 +323,42 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t yph = 0;
       int last[4] = {-1, -1, -1, -1}, ylast[2] = {-1, -1};
       bool ok = true, skipped = false;
-      for (int64_t t = t_begin; t < t_end && ok; ++t, ph ^= 1) {
+      // Tile sequence: a contiguous static range (the dY accumulator stays in TMEM across a
+      // segment), then tiles claimed one at a time, so CTAs that run fast take more of the tail.
+      const int64_t jsub = blockIdx.x % a.group, sub = blockIdx.x / a.group;
+      const int64_t subs = gridDim.x / a.group;
+      int64_t s_next = a.static_rows * sub / subs;
+      const int64_t s_end = a.static_rows * (sub + 1) / subs;
+      const int64_t dyn_base = a.static_rows * a.group;
+      bool exhausted = false;
+      auto fetch = [&]() -> int64_t {
+        if (s_next < s_end) return (s_next++) * a.group + jsub;
+        if (exhausted || dyn_base >= a.total_tiles) return -1;
+        const int64_t t = dyn_base + (int64_t)atomicAdd(a.counter, 1);
+        if (t >= a.total_tiles) {
+          exhausted = true;
+          return -1;
+        }
+        return t;
+      };
+      int pslot = 0;
+      uint32_t pph = 0;
+      auto publish = [&](int64_t t, bool seg_end) -> bool {
+        if (!ptx::mbar_wait_bounded(&sq_empty[pslot], pph ^ 1, a.status, a.timeout_ns)) return false;
+        sq_tile[pslot] = t;
+        sq_seg_end[pslot] = seg_end ? 1 : 0;
+        ptx::mbar_arrive(&sq_full[pslot]);
+        if (++pslot == SQ) {
+          pslot = 0;
+          pph ^= 1;
+        }
+        return true;
+      };
+      int64_t t = fetch();
+      for (; t >= 0 && ok; ph ^= 1) {
         const TileCoord tc = tile_of(t, a);
+        const int64_t nxt = fetch();
+        if (!publish(t, nxt < 0 || !same_segment(tile_of(nxt, a), tc))) { ok = false; break; }
         const int i0 = tc.ib * BT, j0 = tc.jb * BT, d0 = tc.slice * DS;
         for (int s = 0; s < 4; ++s) {
           if (!ptx::mbar_wait_bounded(&empty[s], ph ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
@@ -288,6 +375,13 @@ __global__ void __launch_bounds__(THREADS, 1)
           // Y rows of the strip's 32 columns (B operand of the dX product).
           if (!ptx::mbar_wait_bounded(&yempty[yst], yph ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
           uint8_t* ym = yring + yst * 2 * C::X_BYTES;
+#ifdef RBF_TRACE
+          if (a.ablate & 64) {
+            ptx::mbar_arrive(&yfull[yst]);
+            if (++yst == YSTAGES) { yst = 0; yph ^= 1; }
+            continue;
+          }
+#endif
           ptx::mbar_arrive_expect_tx(&yfull[yst], 2 * C::X_BYTES);
 #pragma unroll
           for (int b = 0; b < DS / 32; ++b) {
@@ -298,7 +392,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           ylast[yst] = (int)yph;
           if (++yst == YSTAGES) { yst = 0; yph ^= 1; }
         }
+        t = nxt;
       }
+      if (ok && !publish(-1, true)) ok = false;
       if (!ok) {  // let every copy this thread issued land before the CTA exits
         for (int s = 0; s < 4; ++s)
           if (last[s] >= 0) ptx::mbar_wait_bounded(&full[s], (uint32_t)last[s], a.status, a.timeout_ns);
@@ -314,12 +410,23 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t xph = 0;
       int xlast[2] = {-1, -1};
       bool ok = true;
-      for (int64_t t = t_begin; t < t_end && ok; ++t) {
+      while (ok) {
+        int64_t t;
+        bool seg_end;
+        if (!sched_pop(sq, false, a, t, seg_end)) { ok = false; break; }
+        if (t < 0) break;
         const TileCoord tc = tile_of(t, a);
         const int i0 = tc.ib * BT, d0 = tc.slice * DS;
         for (int s = 0; s < 4; ++s) {
           if (!ptx::mbar_wait_bounded(&xempty[xst], xph ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
           uint8_t* xm = xring + xst * 2 * C::X_BYTES;
+#ifdef RBF_TRACE
+          if (a.ablate & 64) {
+            ptx::mbar_arrive(&xfull[xst]);
+            if (++xst == XSTAGES) { xst = 0; xph ^= 1; }
+            continue;
+          }
+#endif
           ptx::mbar_arrive_expect_tx(&xfull[xst], 2 * C::X_BYTES);
 #pragma unroll
           for (int b = 0; b < DS / 32; ++b) {
@@ -345,7 +452,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t wt_ph[2] = {0, 0};
       bool ok = true, dy_first = true;
       TileCoord cur = {-1, -1, -1};
-      for (int64_t t = t_begin; t < t_end && ok; ++t) {
+      while (ok) {
+        int64_t t;
+        bool seg_end;
+        if (!sched_pop(sq, false, a, t, seg_end)) { ok = false; break; }
+        if (t < 0) break;
         const TileCoord tc = tile_of(t, a);
         if (!same_segment(tc, cur)) {
           cur = tc;
@@ -354,14 +465,15 @@ __global__ void __launch_bounds__(THREADS, 1)
           dye_ph ^= 1;
           dy_first = true;
         }
-        TRACE(2, 10);
         for (int s = 0; s < 4 && ok; ++s) {
           const int h = s >> 1;  // W^T half: rows 64h .. 64h+63
           if ((s & 1) == 0) {
             if (!ptx::mbar_wait_bounded(&wt_full[h], wt_ph[h], a.status, a.timeout_ns)) { ok = false; break; }
+            TRACE(2, 10 + h);
             wt_ph[h] ^= 1;
           }
           if (!ptx::mbar_wait_bounded(&xfull[xs], xph, a.status, a.timeout_ns)) { ok = false; break; }
+          TRACE(2, 20 + s);
           ptx::tc_fence_after();
           const uint32_t xb = ptx::smem_u32(xring + xs * 2 * C::X_BYTES);
           const uint32_t at = tmem + COL_WT + SR * s;
@@ -369,6 +481,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int k = 0; k < SR / 8; ++k) {
             const uint64_t bh = ptx::smem_desc(xb + 1024 * k, BOX, MN_SBO, MN_LAYOUT);
             const uint64_t bl = ptx::smem_desc(xb + C::X_BYTES + 1024 * k, BOX, MN_SBO, MN_LAYOUT);
+#ifdef RBF_TRACE
+            if (a.ablate & 16) continue;
+#endif
             ptx::mma_tf32_ts(tmem + COL_DY, at + 8 * k, bh, idesc, dy_first ? 0u : 1u);
             ptx::mma_tf32_ts(tmem + COL_DY, at + 8 * k, bl, idesc, 1);
             ptx::mma_tf32_ts(tmem + COL_DY, at + 128 + 8 * k, bh, idesc, 1);
@@ -379,7 +494,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (++xs == XSTAGES) { xs = 0; xph ^= 1; }
         }
         if (!ok) break;
-        if (segment_ends(t, t_end, tc, a)) ptx::mma_commit(dy_full);
+        if (seg_end) ptx::mma_commit(dy_full);
       }
       ptx::mma_commit(drain);  // every MMA this thread issued must finish before TMEM is freed
       ptx::mbar_wait_bounded(drain, 0, a.status, a.timeout_ns);
@@ -389,7 +504,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t yph = 0, dxe_ph = 0;
       uint32_t w_ph[2] = {0, 0};
       bool ok = true;
-      for (int64_t t = t_begin; t < t_end && ok; ++t) {
+      while (ok) {
+        int64_t t;
+        bool seg_end;
+        if (!sched_pop(sq, false, a, t, seg_end)) { ok = false; break; }
+        if (t < 0) break;
         // The R-warps drained the accumulator of the previous tile.
         if (!ptx::mbar_wait_bounded(dx_empty, dxe_ph ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
         dxe_ph ^= 1;
@@ -397,7 +516,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (!ptx::mbar_wait_bounded(&w_full[wb], w_ph[wb], a.status, a.timeout_ns) ||
               !ptx::mbar_wait_bounded(&yfull[ys], yph, a.status, a.timeout_ns)) { ok = false; break; }
           w_ph[wb] ^= 1;
-          TRACE(2, 20 + s);
+          TRACE(3, 20 + s);
           ptx::tc_fence_after();
           const uint32_t aw = tmem + COL_W + 64 * wb;
           const uint32_t yb = ptx::smem_u32(yring + ys * 2 * C::X_BYTES);
@@ -405,6 +524,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int k = 0; k < SR / 8; ++k) {
             const uint64_t bh = ptx::smem_desc(yb + 1024 * k, BOX, MN_SBO, MN_LAYOUT);
             const uint64_t bl = ptx::smem_desc(yb + C::X_BYTES + 1024 * k, BOX, MN_SBO, MN_LAYOUT);
+#ifdef RBF_TRACE
+            if (a.ablate & 16) continue;
+#endif
             ptx::mma_tf32_ts(tmem + COL_DX, aw + 8 * k, bh, idesc, (s | k) != 0 ? 1u : 0u);
             ptx::mma_tf32_ts(tmem + COL_DX, aw + 8 * k, bl, idesc, 1);
             ptx::mma_tf32_ts(tmem + COL_DX, aw + 32 + 8 * k, bh, idesc, 1);
@@ -435,14 +557,18 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t coff[8];
 #pragma unroll
     for (int r = 0; r < 8; ++r) coff[r] = (((lane >> 2) ^ r) << 4) + (lane & 3) * 4;
-    for (int64_t t = t_begin; t < t_end && ok; ++t, ph ^= 1) {
+    for (; ok; ph ^= 1) {
+      int64_t t;
+      bool seg_end;
+      if (!sched_pop(sq, true, a, t, seg_end)) { ok = false; break; }
+      if (t < 0) break;
       const TileCoord tc = tile_of(t, a);
       if (!same_segment(tc, cur)) {
         cur = tc;
         colsum = 0.f;
       }
       if (!ptx::mbar_wait_bounded(&full[q], ph, a.status, a.timeout_ns)) { ok = false; break; }
-      if (lane == 0 && q == 0) TRACE(3, 10);
+      if (lane == 0 && (q == 0 || q == 3)) TRACE(q == 0 ? 4 : 6, 10);
       const uint8_t* gb = ring + q * 2 * STRIP;
       const uint8_t* kb = gb + STRIP;
 #pragma unroll 1
@@ -450,9 +576,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         // This half of the W^T tile was read by the previous tile's dY MMAs.
         if (!ptx::mbar_wait_bounded(&wt_empty[h], wte_ph[h] ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
         wte_ph[h] ^= 1;
+        if (lane == 0 && q == 0) TRACE(4, 20 + h);
         ptx::tc_fence_after();
 #pragma unroll 1
         for (int r0 = 64 * h; r0 < 64 * h + 64; r0 += 32) {
+#ifdef RBF_TRACE
+          if (a.ablate & 4) break;
+#endif
           uint32_t hi[32], lo[32];
 #pragma unroll
           for (int r = 0; r < 32; ++r) {
@@ -472,11 +602,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&wt_full[h]);
+        if (lane == 0 && q == 0) TRACE(4, 30 + h);
       }
       if (!ok) break;
       if (lane == 0) ptx::mbar_arrive(&empty[q]);
-      if (lane == 0 && q == 0) TRACE(3, 30);
-      if (segment_ends(t, t_end, tc, a)) {
+      if (lane == 0 && (q == 0 || q == 3)) TRACE(q == 0 ? 4 : 6, 40);
+      if (seg_end) {
         if (!ptx::mbar_wait_bounded(dy_full, dyf_ph, a.status, a.timeout_ns)) { ok = false; break; }
         dyf_ph ^= 1;
         ptx::tc_fence_after();
@@ -486,7 +617,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(dy_empty);
         const int64_t j = (int64_t)tc.jb * BT + q * 32 + lane;
+#ifdef RBF_TRACE
+        if (a.ablate & 32) continue;
+#endif
         if (j < a.M) flush_row<DS>(a.dY, a.Y, j, a.D, tc.slice * DS, a.c, colsum, accv);
+        if (lane == 0 && q == 0) TRACE(4, 50);
       }
     }
   } else {
@@ -542,18 +677,25 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       return true;
     };
-    for (int64_t t = t_begin; t < t_end && ok; ++t, ph ^= 1) {
+    for (; ok; ph ^= 1) {
+      int64_t t;
+      bool seg_end;
+      if (!sched_pop(sq, true, a, t, seg_end)) { ok = false; break; }
+      if (t < 0) break;
       const TileCoord tc = tile_of(t, a);
       float rowsum = 0.f;
       for (int s = 0; s < 4; ++s) {
         if (!ptx::mbar_wait_bounded(&full[s], ph, a.status, a.timeout_ns)) { ok = false; break; }
-        if (lane == 0 && q == 0) TRACE(4, 10 + s);
+        if (lane == 0 && (q == 0 || q == 3)) TRACE(q == 0 ? 5 : 7, 10 + s);
         // Row (32q + lane) of strip s: its 32 columns in 128 swizzled bytes.
         const uint8_t* gb = ring + s * 2 * STRIP + (q * 32 + lane) * 128;
         const uint8_t* kb = gb + STRIP;
         uint32_t hi[32], lo[32];
 #pragma unroll
         for (int c4 = 0; c4 < 8; ++c4) {
+#ifdef RBF_TRACE
+          if (a.ablate & 8) { hi[4 * c4] = hi[4 * c4 + 1] = hi[4 * c4 + 2] = hi[4 * c4 + 3] = 0u; lo[4 * c4] = lo[4 * c4 + 1] = lo[4 * c4 + 2] = lo[4 * c4 + 3] = 0u; continue; }
+#endif
           const int off = (c4 ^ (lane & 7)) << 4;
           const float4 g = *reinterpret_cast<const float4*>(gb + off);
           const float4 k = *reinterpret_cast<const float4*>(kb + off);
@@ -571,19 +713,26 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) ptx::mbar_arrive(&empty[s]);
         if (!ptx::mbar_wait_bounded(&w_empty[wb], we_ph[wb] ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
         we_ph[wb] ^= 1;
+        if (lane == 0 && q == 0) TRACE(5, 20 + s);
         ptx::tc_fence_after();
+#ifdef RBF_TRACE
+        if (!(a.ablate & 8)) {
+#endif
         ptx::tmem_st32(tmem + lane_base + COL_W + 64 * wb, hi);
         ptx::tmem_st32(tmem + lane_base + COL_W + 64 * wb + 32, lo);
         ptx::tmem_wait_st();
+#ifdef RBF_TRACE
+        }
+#endif
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&w_full[wb]);
-        if (lane == 0 && q == 0) TRACE(4, 30 + s);
+        if (lane == 0 && q == 0) TRACE(5, 30 + s);
         wb ^= 1;
         if (s == 0 && pending) {
           if (!flush_prev()) { ok = false; break; }
           pending = false;
-          if (lane == 0 && q == 0) TRACE(4, 40);
+          if (lane == 0 && q == 0) TRACE(5, 40);
         }
       }
       if (!ok) break;
@@ -651,9 +800,12 @@ __global__ void __launch_bounds__(256) rbf_bwd_zero_kernel(float* __restrict__ a
 
 }  // namespace
 
+// Scratch after the split-pass layout: the rowsum vector [N] and the tile counter.
+static int64_t rowsum_bytes(int64_t N) { return round_up((int64_t)sizeof(float) * N, (int64_t)kAlign); }
+
 size_t backward_scratch_bytes(int64_t N, int64_t M, int64_t D) {
   (void)M; (void)D;
-  return (size_t)round_up((int64_t)sizeof(float) * N, (int64_t)kAlign);
+  return (size_t)(rowsum_bytes(N) + kAlign);
 }
 
 bool backward_tc_supported(int64_t N, int64_t M, int64_t D) {
@@ -668,14 +820,17 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
   const PrepLayout L = prep_layout(N, M, D);
   const bool tma_flush = (D % 4) == 0;  // dX rows 16-byte pitched
   float* rowsum = ws_at<float>(ws, L.end);
+  int* counter = ws_at<int>(ws, L.end + rowsum_bytes(N));
   const bool work = N > 0 && M > 0 && D > 0;
   {
-    const int64_t nr = (work && tma_flush) ? N : 0;
-    const int64_t total = N * D + M * D + nr;
+    // rowsum and the counter are adjacent: one range covers both (or just the counter).
+    float* zc = (work && tma_flush) ? rowsum : reinterpret_cast<float*>(counter);
+    const int64_t nz = (work && tma_flush) ? rowsum_bytes(N) / 4 + 1 : (work ? 1 : 0);
+    const int64_t total = N * D + M * D + nz;
     if (total > 0) {
       const int64_t blocks = std::min<int64_t>(ceil_div(total, 256), 4 * device_sm_count());
       if ((e = launch_kernel(rbf_bwd_zero_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, dX,
-                             N * D, dY, M * D, rowsum, nr)) != cudaSuccess)
+                             N * D, dY, M * D, zc, nz)) != cudaSuccess)
         return e;
       note_launches(1);
     }
@@ -709,6 +864,19 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
   a.tiles_j = (int)ceil_div(M, BT);
   a.num_slices = (int)ceil_div(L.Dp, DS);
   a.total_tiles = (int64_t)a.tiles_i * a.tiles_j * a.num_slices;
+  a.counter = counter;
+  const int grid = (int)std::min<int64_t>(a.total_tiles, device_sm_count());
+  {
+    // Group width (RBF_BWD_GROUP, default 4) and the share of tiles handed out dynamically
+    // (RBF_BWD_DYN_PCT, default 30).
+    int group = 4, pct = 30;
+    if (const char* s = std::getenv("RBF_BWD_GROUP")) group = std::max(1, std::atoi(s));
+    if (const char* s = std::getenv("RBF_BWD_DYN_PCT")) pct = std::max(0, std::min(100, std::atoi(s)));
+    if (a.tiles_j % group != 0 || grid % group != 0 || grid < group) group = 1;
+    a.group = group;
+    const int64_t rows = a.total_tiles / group;
+    a.static_rows = rows - rows * pct / 100;
+  }
   a.c = -2.f * gamma;
   a.status = ws_at<int>(ws, L.status);
   a.timeout_ns = wc.timeout_ns;
@@ -717,7 +885,6 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
 #ifdef RBF_TRACE
   if (const char* ab = std::getenv("RBF_ABLATE")) a.ablate = std::atoi(ab);
 #endif
-  const int grid = (int)std::min<int64_t>(a.total_tiles, device_sm_count());
   if (DS == 32) {
     if ((e = cudaFuncSetAttribute(rbf_bwd_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)Cfg<32>::SMEM)) != cudaSuccess)
