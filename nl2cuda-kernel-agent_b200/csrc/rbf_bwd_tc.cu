@@ -175,6 +175,10 @@ __device__ __forceinline__ bool sched_pop(SchedRing& r, bool whole_warp, const B
   return true;
 }
 
+// Per-buffer mbarrier parities packed into one register (bit k = buffer k), so that indexing by
+// a run-time buffer number does not put a small array in local memory.
+__device__ __forceinline__ uint32_t bit_of(uint32_t bits, int k) { return (bits >> k) & 1u; }
+
 __device__ __forceinline__ void red_add4(float* p, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
                "f"(d)
@@ -321,7 +325,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t ph = 0;  // strip stage parity: flips once per tile
       int yst = 0;
       uint32_t yph = 0;
-      int last[4] = {-1, -1, -1, -1}, ylast[2] = {-1, -1};
+      uint32_t issued = 0, last = 0;  // strip stages with a load in flight and their parities
+      uint32_t yissued = 0, ylast = 0;
       bool ok = true, skipped = false;
       // Tile sequence: a contiguous static range (the dY accumulator stays in TMEM across a
       // segment), then tiles claimed one at a time, so CTAs that run fast take more of the tail.
@@ -370,7 +375,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             ptx::mbar_arrive_expect_tx(&full[s], 2 * STRIP);
             ptx::tma_load_2d_hint(sm, &tm_g, j0 + SR * s, i0, &full[s], stream);
             ptx::tma_load_2d_hint(sm + STRIP, &tm_k, j0 + SR * s, i0, &full[s], stream);
-            last[s] = (int)ph;
+            issued |= 1u << s;
+            last = (last & ~(1u << s)) | (ph << s);
           }
           // Y rows of the strip's 32 columns (B operand of the dX product).
           if (!ptx::mbar_wait_bounded(&yempty[yst], yph ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
@@ -389,7 +395,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             ptx::tma_load_2d_hint(ym + C::X_BYTES + b * BOX, &tm_ylo, d0 + 32 * b, j0 + SR * s,
                                   &yfull[yst], keep);
           }
-          ylast[yst] = (int)yph;
+          yissued |= 1u << yst;
+          ylast = (ylast & ~(1u << yst)) | (yph << yst);
           if (++yst == YSTAGES) { yst = 0; yph ^= 1; }
         }
         t = nxt;
@@ -397,9 +404,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (ok && !publish(-1, true)) ok = false;
       if (!ok) {  // let every copy this thread issued land before the CTA exits
         for (int s = 0; s < 4; ++s)
-          if (last[s] >= 0) ptx::mbar_wait_bounded(&full[s], (uint32_t)last[s], a.status, a.timeout_ns);
+          if (issued >> s & 1u) ptx::mbar_wait_bounded(&full[s], bit_of(last, s), a.status, a.timeout_ns);
         for (int s = 0; s < 2; ++s)
-          if (ylast[s] >= 0) ptx::mbar_wait_bounded(&yfull[s], (uint32_t)ylast[s], a.status, a.timeout_ns);
+          if (yissued >> s & 1u) ptx::mbar_wait_bounded(&yfull[s], bit_of(ylast, s), a.status, a.timeout_ns);
       }
     }
   } else if (warp == 1) {
@@ -408,7 +415,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint64_t keep = ptx::policy_evict_last();
       int xst = 0;
       uint32_t xph = 0;
-      int xlast[2] = {-1, -1};
+      uint32_t xissued = 0, xlast = 0;
       bool ok = true;
       while (ok) {
         int64_t t;
@@ -434,13 +441,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             ptx::tma_load_2d_hint(xm + C::X_BYTES + b * BOX, &tm_xlo, d0 + 32 * b, i0 + SR * s,
                                   &xfull[xst], keep);
           }
-          xlast[xst] = (int)xph;
+          xissued |= 1u << xst;
+          xlast = (xlast & ~(1u << xst)) | (xph << xst);
           if (++xst == XSTAGES) { xst = 0; xph ^= 1; }
         }
       }
       if (!ok)
         for (int s = 0; s < 2; ++s)
-          if (xlast[s] >= 0) ptx::mbar_wait_bounded(&xfull[s], (uint32_t)xlast[s], a.status, a.timeout_ns);
+          if (xissued >> s & 1u) ptx::mbar_wait_bounded(&xfull[s], bit_of(xlast, s), a.status, a.timeout_ns);
     }
   } else if (warp == 2 || warp == 3) {
     // ================================================================ MMA issuers
@@ -449,7 +457,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // ---- dY: once per tile, A = W^T (TMEM lanes j, K = 128 rows i), B = X rows in 4 chunks.
       int xs = 0;
       uint32_t xph = 0, dye_ph = 0;
-      uint32_t wt_ph[2] = {0, 0};
+      uint32_t wt_ph = 0;  // parity bits of wt_full[0..1]
       bool ok = true, dy_first = true;
       TileCoord cur = {-1, -1, -1};
       while (ok) {
@@ -468,9 +476,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int s = 0; s < 4 && ok; ++s) {
           const int h = s >> 1;  // W^T half: rows 64h .. 64h+63
           if ((s & 1) == 0) {
-            if (!ptx::mbar_wait_bounded(&wt_full[h], wt_ph[h], a.status, a.timeout_ns)) { ok = false; break; }
+            if (!ptx::mbar_wait_bounded(&wt_full[h], bit_of(wt_ph, h), a.status, a.timeout_ns)) { ok = false; break; }
             TRACE(2, 10 + h);
-            wt_ph[h] ^= 1;
+            wt_ph ^= 1u << h;
           }
           if (!ptx::mbar_wait_bounded(&xfull[xs], xph, a.status, a.timeout_ns)) { ok = false; break; }
           TRACE(2, 20 + s);
@@ -502,7 +510,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // ---- dX: per strip, A = W (TMEM lanes i, K = 32 columns j), B = the strip's Y rows.
       int ys = 0, wb = 0;
       uint32_t yph = 0, dxe_ph = 0;
-      uint32_t w_ph[2] = {0, 0};
+      uint32_t w_ph = 0;  // parity bits of w_full[0..1]
       bool ok = true;
       while (ok) {
         int64_t t;
@@ -513,9 +521,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!ptx::mbar_wait_bounded(dx_empty, dxe_ph ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
         dxe_ph ^= 1;
         for (int s = 0; s < 4 && ok; ++s) {
-          if (!ptx::mbar_wait_bounded(&w_full[wb], w_ph[wb], a.status, a.timeout_ns) ||
+          if (!ptx::mbar_wait_bounded(&w_full[wb], bit_of(w_ph, wb), a.status, a.timeout_ns) ||
               !ptx::mbar_wait_bounded(&yfull[ys], yph, a.status, a.timeout_ns)) { ok = false; break; }
-          w_ph[wb] ^= 1;
+          w_ph ^= 1u << wb;
           TRACE(3, 20 + s);
           ptx::tc_fence_after();
           const uint32_t aw = tmem + COL_W + 64 * wb;
@@ -549,7 +557,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int q = warp & 3;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     uint32_t ph = 0, dyf_ph = 0;
-    uint32_t wte_ph[2] = {0, 0};
+    uint32_t wte_ph = 0;  // parity bits of wt_empty[0..1]
     float colsum = 0.f;
     TileCoord cur = {-1, -1, -1};
     bool ok = true;
@@ -574,8 +582,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
       for (int h = 0; h < 2 && ok; ++h) {
         // This half of the W^T tile was read by the previous tile's dY MMAs.
-        if (!ptx::mbar_wait_bounded(&wt_empty[h], wte_ph[h] ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
-        wte_ph[h] ^= 1;
+        if (!ptx::mbar_wait_bounded(&wt_empty[h], bit_of(wte_ph, h) ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
+        wte_ph ^= 1u << h;
         if (lane == 0 && q == 0) TRACE(4, 20 + h);
         ptx::tc_fence_after();
 #pragma unroll 1
@@ -632,7 +640,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     int wb = 0;
     uint32_t ph = 0, dxf_ph = 0;
-    uint32_t we_ph[2] = {0, 0};
+    uint32_t we_ph = 0;  // parity bits of w_empty[0..1]
     bool ok = true, pending = false;
     float prev_rowsum = 0.f;
     int64_t prev_i = 0;
@@ -711,8 +719,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&empty[s]);
-        if (!ptx::mbar_wait_bounded(&w_empty[wb], we_ph[wb] ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
-        we_ph[wb] ^= 1;
+        if (!ptx::mbar_wait_bounded(&w_empty[wb], bit_of(we_ph, wb) ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
+        we_ph ^= 1u << wb;
         if (lane == 0 && q == 0) TRACE(5, 20 + s);
         ptx::tc_fence_after();
 #ifdef RBF_TRACE

@@ -169,8 +169,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t a_full_c = PAIR ? ptx::map_to_rank(a_full, 0) : 0;
       int stage = 0;
       uint32_t phase = 0, a_phase = 0;
-      int last_parity[NS], a_issued = -1;
-      for (int s = 0; s < NS; ++s) last_parity[s] = -1;
+      // Stages with a load in flight and their parities, as bit masks (no local-memory array).
+      uint32_t issued = 0, last = 0;
+      int a_issued = -1;
       bool ok = true, skipped = false;
       int cur_ib = -1;
       for (int64_t t = t_begin; t < t_end && ok; ++t) {
@@ -209,7 +210,10 @@ __global__ void __launch_bounds__(THREADS, 1)
               ptx::tma_load_2d(bm, &tm_yhi, kc * BK, j0, &full[stage]);
               ptx::tma_load_2d(bm + BSTAGE / 2, &tm_ylo, kc * BK, j0, &full[stage]);
             }
-            if (leader) last_parity[stage] = (int)phase;
+            if (leader) {
+              issued |= 1u << stage;
+              last = (last & ~(1u << stage)) | (phase << stage);
+            }
           }
           if (++stage == NS) { stage = 0; phase ^= 1; }
         }
@@ -218,15 +222,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       // barriers count both CTAs' bytes, and the final cluster barrier holds the peer until then).
       if (!ok) {
         for (int s = 0; s < NS; ++s)
-          if (last_parity[s] >= 0)
-            ptx::mbar_wait_bounded(&full[s], (uint32_t)last_parity[s], a.status, a.timeout_ns);
+          if (issued >> s & 1u)
+            ptx::mbar_wait_bounded(&full[s], (last >> s) & 1u, a.status, a.timeout_ns);
         if (a_issued >= 0) ptx::mbar_wait_bounded(a_full, (uint32_t)a_issued, a.status, a.timeout_ns);
       }
     } else if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      int last_parity[STAGES];
-      for (int s = 0; s < STAGES; ++s) last_parity[s] = -1;
+      uint32_t issued = 0, last = 0;
       bool ok = true;
       bool skipped = false;
       for (int64_t t = t_begin; t < t_end && ok; ++t) {
@@ -246,7 +249,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             ptx::tma_load_2d(sm + TILE_BYTES, &tm_xlo, kc * BK, i0, &full[stage]);
             ptx::tma_load_2d(sm + 2 * TILE_BYTES, &tm_yhi, kc * BK, j0, &full[stage]);
             ptx::tma_load_2d(sm + 3 * TILE_BYTES, &tm_ylo, kc * BK, j0, &full[stage]);
-            last_parity[stage] = (int)phase;
+            issued |= 1u << stage;
+            last = (last & ~(1u << stage)) | (phase << stage);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -257,8 +261,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!ok) {
         // Error path: let every load this thread issued land before the CTA exits.
         for (int s = 0; s < STAGES; ++s)
-          if (last_parity[s] >= 0)
-            ptx::mbar_wait_bounded(&full[s], (uint32_t)last_parity[s], a.status, a.timeout_ns);
+          if (issued >> s & 1u)
+            ptx::mbar_wait_bounded(&full[s], (last >> s) & 1u, a.status, a.timeout_ns);
       }
     }
   } else if (warp == 1) {

@@ -55,8 +55,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Slow path of mbar_wait_bounded, kept out of line so that the many wait sites of the
 // persistent kernels share one copy of the polling loop (instruction-cache footprint).
-static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* status,
-                                            uint64_t timeout_ns) {
+#ifdef RBF_WAIT_INLINE
+static __device__ __forceinline__ bool mbar_wait_slow(
+#else
+static __device__ __noinline__ bool mbar_wait_slow(
+#endif
+    uint64_t* bar, uint32_t parity, int* status, uint64_t timeout_ns) {
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
