@@ -205,12 +205,13 @@ def cpu_baseline(c, seconds):
     N, M, D, g = c["N_global"], c["M"], c["D"], c["gamma"]
     probe_s, _ = reference_port.time_sample(N, M, D, g, 16, threads)
     rows = int(max(16, min(N, 16 * seconds / max(probe_s, 1e-3) / 2)))
-    sec, done = reference_port.time_sample(N, M, D, g, rows, threads)
+    # Repeat the sample (at most all N rows per pass) until about `seconds` of CPU work.
+    sec, done = reference_port.time_sample(N, M, D, g, rows, threads, min_seconds=0.75 * seconds)
     torch.set_num_threads(threads)
     return {"value": round(6.0 * done * M * D / sec / 1e9, 3), "unit": UNIT, "cores": threads,
             "kind": "port",
-            "sample": f"{done} of {N} rows of X x all {M} rows of Y, fwd+bwd "
-                      f"({sec:.1f} s on {threads} threads)"}
+            "sample": f"{done} rows of X ({rows} per pass, of {N}) x all {M} rows of Y, "
+                      f"fwd+bwd ({sec:.1f} s on {threads} threads)"}
 
 
 def main():

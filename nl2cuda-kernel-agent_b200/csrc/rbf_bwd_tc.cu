@@ -224,6 +224,19 @@ __device__ __forceinline__ void tmem_load_row(uint32_t taddr, uint32_t (&v)[64])
   ptx::tmem_wait_ld();
 }
 
+// Store N (8, 16 or 32) consecutive TMEM columns of this thread's lane.
+template <int N>
+__device__ __forceinline__ void tmem_st_n(uint32_t taddr, const uint32_t* r) {
+  if (N == 8) ptx::tmem_st8(taddr, r);
+  else if (N == 16) ptx::tmem_st16(taddr, r);
+  else ptx::tmem_st32(taddr, *reinterpret_cast<const uint32_t(*)[32]>(r));
+}
+
+#ifndef RBF_CB
+#define RBF_CB 8
+#endif
+constexpr int CB = RBF_CB;  // rows of W^T a C-warp converts per TMEM store (code size vs. batching)
+
 template <int DS>
 __global__ void __launch_bounds__(THREADS, 1)
     rbf_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_g,
@@ -587,13 +600,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0 && q == 0) TRACE(4, 20 + h);
         ptx::tc_fence_after();
 #pragma unroll 1
-        for (int r0 = 64 * h; r0 < 64 * h + 64; r0 += 32) {
+        for (int r0 = 64 * h; r0 < 64 * h + 64; r0 += CB) {
 #ifdef RBF_TRACE
           if (a.ablate & 4) break;
 #endif
-          uint32_t hi[32], lo[32];
+          uint32_t hi[CB], lo[CB];
 #pragma unroll
-          for (int r = 0; r < 32; ++r) {
+          for (int r = 0; r < CB; ++r) {
             const uint32_t off = (uint32_t)(r0 + r) * 128 + coff[r & 7];
             const float w = *reinterpret_cast<const float*>(gb + off) *
                             *reinterpret_cast<const float*>(kb + off);
@@ -603,8 +616,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             hi[r] = __float_as_uint(hh);
             lo[r] = __float_as_uint(ll);
           }
-          ptx::tmem_st32(tmem + lane_base + COL_WT + r0, hi);
-          ptx::tmem_st32(tmem + lane_base + COL_WT + 128 + r0, lo);
+          tmem_st_n<CB>(tmem + lane_base + COL_WT + r0, hi);
+          tmem_st_n<CB>(tmem + lane_base + COL_WT + 128 + r0, lo);
         }
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
