@@ -10,7 +10,9 @@ gradient G, fp32 in and out.  FLOP per step = 6*N*M*D; algorithmic HBM bytes per
 
 N = 1 runs config c1 (N=M=4096, D=64).  Under torchrun (WORLD_SIZE = N > 1) the work is
 weak-scaled by rows: every rank owns 4096 rows of X (and of G, K), Y (4096 x 64) is replicated,
-and the partial dY is summed with one NCCL all-reduce per step ("scaling": "weak").
+and the partial dY is reduced inside the backward over NVLink peer memory (the dY partials go
+straight into the owning rank's buffer, then one bounded cross-GPU barrier and a gather;
+RBF_DY_REDUCE=nccl uses one NCCL all-reduce instead) ("scaling": "weak").
 ``value`` = whole-job GFLOP/s = (6 * N_global * M * D) / (max over ranks of the device time of
 one step).  Inputs are resident in HBM when timing starts; L2 is flushed (256 MiB write) before
 every timed step, outside the events.
@@ -244,9 +246,15 @@ def main():
                     generator=torch.Generator(device=dev).manual_seed(777 + rank))
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     compute = shard.NativeShardCompute()
+    route = None
+    dy_reduce = "none"
+    if world > 1:
+        dy_reduce = os.environ.get("RBF_DY_REDUCE", "peer")
+        if dy_reduce == "peer":
+            route = shard.RoutedDy(M, D, dev)
 
     def step():
-        return shard.forward_backward_shard(X, Y, G, g, compute=compute)
+        return shard.forward_backward_shard(X, Y, G, g, compute=compute, route=route)
 
     for _ in range(max(args.warmup, 0)):
         step()
@@ -339,7 +347,7 @@ def main():
     # End to end through the public API with host buffers.
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(X, Y, G, g, world, dev, args, shard, op)
+        e2e = run_e2e(X, Y, G, g, world, dev, args, shard, op, route)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -355,8 +363,10 @@ def main():
                                    f"(N={Ng} total), M={M}, D={D}, gamma={g:.6g}",
                        "N": Ng, "M": M, "D": D, "rows_per_rank": n,
                        "l2": "flushed before every timed step (256 MiB write, outside events)",
-                       "parallelism": f"row-shard x{world}" + (", dY all-reduce (NCCL)"
-                                                              if world > 1 else "")},
+                       "parallelism": f"row-shard x{world}" + (
+                           ", dY reduced in the backward over NVLink peer memory"
+                           if dy_reduce == "peer" else ", dY all-reduce (NCCL)"
+                           if world > 1 else "")},
             "ms_fwd": round(ms_fwd, 5), "ms_bwd": round(ms_bwd, 5),
             "pct_roofline_step": round(100.0 * t_roof / (ms * 1e-3), 2),
             "roofline_step_us": round(t_roof * 1e6, 2),
@@ -379,7 +389,7 @@ def main():
         os._exit(0)
 
 
-def run_e2e(X, Y, G, g, world, dev, args, shard, op):
+def run_e2e(X, Y, G, g, world, dev, args, shard, op, route=None):
     """Same metric through the public API, host buffers in and out: per step the H2D copy of
     X (this rank's rows), Y and G from pinned memory, forward + backward, and the D2H copy of
     K, dX and dY into pinned memory, all inside the events."""
@@ -405,7 +415,7 @@ def run_e2e(X, Y, G, g, world, dev, args, shard, op):
             K.backward(Gd)
             dX, dY = Xd.grad, Yd.grad
         else:
-            K, dX, dY = shard.forward_backward_shard(Xd, Yd, Gd, g)
+            K, dX, dY = shard.forward_backward_shard(Xd, Yd, Gd, g, route=route)
         Kh.copy_(K.detach(), non_blocking=True)
         dXh.copy_(dX, non_blocking=True)
         dYh.copy_(dY, non_blocking=True)

@@ -115,6 +115,35 @@ RBF_API int rbf_sm100_backward_shard(const float* X_local, const float* Y, const
                              int64_t N_local, int64_t M, int64_t D, float gamma,
                              void* workspace, size_t workspace_bytes, rbf_stream_t stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Row-sharded backward with the dY all-reduce done by this library over NVLink peer memory.  No
+ * counterpart in the reference (it runs on one GPU); replaces rbf_sm100_backward_shard + an NCCL
+ * all-reduce of dY.  `dy_buffers[r]` is rank r's buffer of 2 * M * D floats, mapped in this
+ * process (peer memory, e.g. CUDA symmetric memory); every rank passes the same list.  The
+ * backward zeroes slot (*step_counter % 2) of dy_buffers[rank] and accumulates this rank's dY
+ * partial there; rbf_sm100_dy_exchange then completes dY.  X_local, G_local, K_local, dX_local,
+ * workspace: as rbf_sm100_backward_prepared (the forward filled the workspace).  M % 4 == 0.
+ * ------------------------------------------------------------------------------------------- */
+RBF_API int rbf_sm100_backward_shard_routed(const float* X_local, const float* Y,
+                                            const float* G_local, const float* K_local,
+                                            float* dX_local, int64_t N_local, int64_t M, int64_t D,
+                                            float gamma, void* workspace, size_t workspace_bytes,
+                                            float* const* dy_buffers, int world, int rank,
+                                            const int* step_counter, rbf_stream_t stream);
+
+/* Completes a routed step on this rank (all ranks call it): barrier; the owner of each 128-row
+ * j-block (j-block % world) sums it over every rank's slot; barrier; the full dY [M, D] is
+ * gathered from the owners; *step_counter advances (device int, 0 on every rank before the first
+ * step).  Both barriers are bounded by RBF_WAIT_TIMEOUT_MS: on expiry the workspace status word
+ * reads RBF_ERR_TIMEOUT, dY is not written and the buffers must be set up again.
+ * `flag_arrays[r]`: rank r's int[world] signal array (peer memory, zeroed once); `tickets`: two
+ * zeroed device unsigned ints of this rank.  D % 4 == 0.  No host synchronisation, so a captured
+ * CUDA graph of the step can be replayed. */
+RBF_API int rbf_sm100_dy_exchange(float* dY, int64_t M, int64_t D, float* const* dy_buffers,
+                                  int* const* flag_arrays, int world, int rank, int* step_counter,
+                                  unsigned* tickets, void* workspace, size_t workspace_bytes,
+                                  rbf_stream_t stream);
+
 /* Status word written by the device-side bounded waits (RBF_OK or RBF_ERR_TIMEOUT).  Blocking:
  * synchronizes `stream`, then copies the word out of `workspace`.  Resets it to RBF_OK. */
 RBF_API int rbf_sm100_read_status(void* workspace, rbf_stream_t stream, int* device_status);

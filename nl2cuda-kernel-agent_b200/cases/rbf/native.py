@@ -48,6 +48,14 @@ def lib():
                 getattr(L, fn).restype = ctypes.c_int
                 getattr(L, fn).argtypes = [_F, _F, _F, _F, _F, _F, _I64, _I64, _I64,
                                            ctypes.c_float, _F, _SZ, _F]
+            L.rbf_sm100_backward_shard_routed.restype = ctypes.c_int
+            L.rbf_sm100_backward_shard_routed.argtypes = [
+                _F, _F, _F, _F, _F, _I64, _I64, _I64, ctypes.c_float, _F, _SZ,
+                ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int, _F, _F]
+            L.rbf_sm100_dy_exchange.restype = ctypes.c_int
+            L.rbf_sm100_dy_exchange.argtypes = [
+                _F, _I64, _I64, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p),
+                ctypes.c_int, ctypes.c_int, _F, _F, _F, _SZ, _F]
             L.rbf_sm100_read_status.restype = ctypes.c_int
             L.rbf_sm100_read_status.argtypes = [_F, _F, ctypes.POINTER(ctypes.c_int)]
             _lib = L
@@ -154,3 +162,35 @@ def read_status(workspace):
     check(lib().rbf_sm100_read_status(_ptr(workspace), _stream(workspace.device),
                                       ctypes.byref(out)), "rbf_sm100_read_status")
     return out.value
+
+
+def rbf_backward_shard_routed(X, Y, G, K, gamma, workspace, route):
+    """dX of this rank's rows; the dY partial is accumulated into this rank's slot of ``route``
+    (a ``shard.RoutedDy``) instead of being returned.  ``workspace`` from
+    ``forward_with_workspace`` of the same X, Y.  Complete the step with ``dy_exchange``."""
+    _check_2d(("X", "Y", "G", "K"), (X, Y, G, K))
+    X, Y, G, K = _operand(X), _operand(Y), _operand(G), _operand(K)
+    N, D = X.shape
+    M = Y.size(0)
+    if Y.size(1) != D or tuple(G.shape) != (N, M) or tuple(K.shape) != (N, M):
+        raise RuntimeError("shape mismatch: need X [N,D], Y [M,D], G and K [N,M]")
+    with torch.cuda.device(X.device):
+        dX = torch.empty_like(X)
+        check(lib().rbf_sm100_backward_shard_routed(
+            _ptr(X), _ptr(Y), _ptr(G), _ptr(K), _ptr(dX), N, M, D, float(gamma), _ptr(workspace),
+            workspace.numel(), route.dy_ptrs, route.world, route.rank, _ptr(route.counters),
+            _stream(X.device)), "rbf_sm100_backward_shard_routed")
+    return dX
+
+
+def dy_exchange(route, workspace, out=None):
+    """Barrier across ranks, then the full dY [M, D] gathered from the owners' slots."""
+    dev = route.device
+    with torch.cuda.device(dev):
+        dY = out if out is not None else torch.empty((route.M, route.D), dtype=torch.float32,
+                                                     device=dev)
+        check(lib().rbf_sm100_dy_exchange(
+            _ptr(dY), route.M, route.D, route.dy_ptrs, route.flag_ptrs, route.world, route.rank,
+            _ptr(route.counters), route.counters.data_ptr() + 4, _ptr(workspace),
+            workspace.numel(), _stream(dev)), "rbf_sm100_dy_exchange")
+    return dY

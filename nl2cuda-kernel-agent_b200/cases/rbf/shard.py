@@ -6,9 +6,10 @@ No reference counterpart (the reference runs on one GPU).  The split:
   * forward: K_r = rbf(X_r, Y) is local, no communication;
   * backward: dX_r is local and complete; dY is linear in the rows, so each rank computes the
     partial dY over its rows and ONE all-reduce (sum) over the process group completes it.
-One process per GPU; the collective is ``torch.distributed.all_reduce`` on the NCCL backend on
-GPUs (NVLink / NVSwitch), gloo on CPU in the tests.  The compute is pluggable so that the same
-driver runs with the sm_100a kernels (``native``) or with a CPU implementation in tests.
+One process per GPU; the collective is either ``torch.distributed.all_reduce`` (NCCL on GPUs,
+gloo on CPU in the tests) or, with ``RoutedDy``, fused into the backward over peer memory.  The
+compute is pluggable so that the same driver runs with the sm_100a kernels (``native``) or with
+a CPU implementation in tests.
 """
 import torch
 import torch.distributed as dist
@@ -34,12 +35,56 @@ class NativeShardCompute:
         return native.rbf_backward(X, Y, G, K, gamma, workspace=state)
 
 
+class RoutedDy:
+    """Peer-memory buffers of the fused dY reduction (no NCCL on the data path).
+
+    Every rank holds, in CUDA symmetric memory, two M x D fp32 slots and an int[world] signal
+    array; the backward accumulates this rank's dY partial into slot ``step % 2``, and
+    ``native.dy_exchange`` completes dY over NVLink peer loads: barrier, each 128-row j-block
+    summed by its owner (j-block % world), barrier, gather from the owners.  ``counters`` (this
+    rank's device ints: step, two tickets) drive the slot choice on the device, so a captured
+    CUDA graph of the step can be replayed.  Build it on every rank of ``group`` (collective).
+    """
+
+    def __init__(self, M, D, device, group=None):
+        import ctypes
+        import torch.distributed._symmetric_memory as symm_mem
+        group = group or dist.group.WORLD
+        self.M, self.D, self.device = int(M), int(D), torch.device(device)
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if not 1 <= self.world <= 8:
+            raise RuntimeError("the fused dY reduction supports 1..8 ranks")
+        if self.D % 4:
+            raise RuntimeError("the fused dY reduction needs D % 4 == 0")
+        slot_bytes = 2 * self.M * self.D * 4
+        self.flags_offset = (slot_bytes + 255) // 256 * 256
+        nbytes = self.flags_offset + 256
+        with torch.cuda.device(self.device):
+            self.buffer = symm_mem.empty(nbytes, dtype=torch.uint8, device=self.device)
+            self.buffer.zero_()
+            self.counters = torch.zeros(4, dtype=torch.int32, device=self.device)
+            torch.cuda.synchronize()
+        self.handle = symm_mem.rendezvous(self.buffer, group)
+        ptrs = [int(p) for p in self.handle.buffer_ptrs]
+        self.dy_ptrs = (ctypes.c_void_p * self.world)(*ptrs)
+        self.flag_ptrs = (ctypes.c_void_p * self.world)(*[p + self.flags_offset for p in ptrs])
+        dist.barrier(group=group)  # every rank's slots and flags are zero before the first step
+
+
 def forward_backward_shard(X_local, Y, G_local, gamma, compute=None, group=None,
-                           reduce_dy=True):
+                           reduce_dy=True, route=None):
     """One forward + backward of this rank's rows.  Returns (K_local, dX_local, dY) where dY is
-    the full gradient (all-reduced over ``group``) when ``reduce_dy`` and the process group is
-    initialised, else this rank's partial sum."""
+    the full gradient when ``reduce_dy`` and the process group is initialised (all-reduced over
+    ``group`` with NCCL, or -- with ``route``, a ``RoutedDy`` -- reduced inside the backward
+    over peer memory), else this rank's partial sum."""
     compute = compute or NativeShardCompute()
+    if route is not None:
+        from cases.rbf import native
+        K_local, ws = native.forward_with_workspace(X_local, Y, gamma)
+        dX_local = native.rbf_backward_shard_routed(X_local, Y, G_local, K_local, gamma, ws, route)
+        dY = native.dy_exchange(route, ws)
+        return K_local, dX_local, dY
     K_local, state = compute.forward(X_local, Y, gamma)
     dX_local, dY = compute.backward(X_local, Y, G_local, K_local, gamma, state)
     if reduce_dy and dist.is_available() and dist.is_initialized():

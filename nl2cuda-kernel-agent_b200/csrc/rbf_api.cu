@@ -132,7 +132,8 @@ int forward_impl(const float* X, const float* Y, float* K, int64_t N, int64_t M,
 
 int backward_impl(const float* X, const float* Y, const float* G, const float* K, float* dX,
                   float* dY, int64_t N, int64_t M, int64_t D, float gamma, void* ws,
-                  size_t ws_bytes, cudaStream_t stream, bool prepared) {
+                  size_t ws_bytes, cudaStream_t stream, bool prepared,
+                  const DyRoute* route = nullptr) {
   int st = check_shape(N, M, D, gamma);
   if (st) return st;
   if ((st = check_ptr(X, N * D, "X"))) return st;
@@ -140,7 +141,7 @@ int backward_impl(const float* X, const float* Y, const float* G, const float* K
   if ((st = check_ptr(G, N * M, "G"))) return st;
   if ((st = check_ptr(K, N * M, "K"))) return st;
   if ((st = check_ptr(dX, N * D, "dX"))) return st;
-  if ((st = check_ptr(dY, M * D, "dY"))) return st;
+  if (route == nullptr && (st = check_ptr(dY, M * D, "dY"))) return st;
   const PrepLayout L = prep_layout(N, M, D);
   const size_t need = L.end + backward_extra_bytes(N, M, D);
   if (ws == nullptr || ws_bytes < need) return set_detail(RBF_ERR_WORKSPACE, "backward workspace too small");
@@ -149,9 +150,11 @@ int backward_impl(const float* X, const float* Y, const float* G, const float* K
   if (!prepared) {
     if ((st = cuda_status(launch_prep(X, Y, N, M, D, ws, stream), "split pass launch"))) return st;
   }
+  if (route != nullptr && !backward_tc_supported(N, M, D))
+    return set_detail(RBF_ERR_UNSUPPORTED, "routed dY needs M % 4 == 0 (tensor-core backward)");
   if (backward_tc_supported(N, M, D))
     return cuda_status(launch_backward_tc(X, Y, G, K, dX, dY, N, M, D, gamma, ws,
-                                          wait_config_from_env(), stream),
+                                          wait_config_from_env(), stream, route),
                        "backward launch");
   return cuda_status(launch_backward_simt(X, Y, G, K, dX, dY, N, M, D, gamma, stream),
                      "backward launch");
@@ -222,6 +225,65 @@ int rbf_sm100_backward_shard(const float* X_local, const float* Y, const float* 
                              size_t workspace_bytes, rbf_stream_t stream) {
   return backward_impl(X_local, Y, G_local, K_local, dX_local, dY_partial, N_local, M, D, gamma,
                        workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), false);
+}
+
+int rbf_sm100_backward_shard_routed(const float* X_local, const float* Y, const float* G_local,
+                                    const float* K_local, float* dX_local, int64_t N_local,
+                                    int64_t M, int64_t D, float gamma, void* workspace,
+                                    size_t workspace_bytes, float* const* dy_buffers, int world,
+                                    int rank, const int* step_counter, rbf_stream_t stream) {
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
+    return set_detail(RBF_ERR_INVALID_ARGUMENT, "world must be in [1, 8] and rank < world");
+  if (dy_buffers == nullptr || step_counter == nullptr)
+    return set_detail(RBF_ERR_INVALID_ARGUMENT, "NULL dY buffers or step counter");
+  DyRoute route{};
+  for (int r = 0; r < world; ++r) {
+    if (dy_buffers[r] == nullptr || !aligned16(dy_buffers[r]))
+      return set_detail(RBF_ERR_MISALIGNED, "dY buffer NULL or not 16-byte aligned");
+    route.bufs[r] = dy_buffers[r];
+  }
+  route.world = world;
+  route.rank = rank;
+  route.ctr = step_counter;
+  return backward_impl(X_local, Y, G_local, K_local, dX_local, nullptr, N_local, M, D, gamma,
+                       workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), true,
+                       &route);
+}
+
+int rbf_sm100_dy_exchange(float* dY, int64_t M, int64_t D, float* const* dy_buffers,
+                          int* const* flag_arrays, int world, int rank, int* step_counter,
+                          unsigned* tickets, void* workspace, size_t workspace_bytes,
+                          rbf_stream_t stream) {
+  if (M < 0 || D < 0) return set_detail(RBF_ERR_INVALID_ARGUMENT, "negative size");
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
+    return set_detail(RBF_ERR_INVALID_ARGUMENT, "world must be in [1, 8] and rank < world");
+  if (dy_buffers == nullptr || flag_arrays == nullptr || step_counter == nullptr ||
+      tickets == nullptr || (dY == nullptr && M * D > 0))
+    return set_detail(RBF_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (D % 4 != 0) return set_detail(RBF_ERR_UNSUPPORTED, "the dY exchange needs D % 4 == 0");
+  if (workspace == nullptr || workspace_bytes < sizeof(int))
+    return set_detail(RBF_ERR_WORKSPACE, "exchange needs the workspace's status word");
+  int st = check_device();
+  if (st) return st;
+  ExchangeArgs a{};
+  a.dY = dY;
+  a.M = M;
+  a.D = D;
+  for (int r = 0; r < world; ++r) {
+    if (dy_buffers[r] == nullptr || flag_arrays[r] == nullptr)
+      return set_detail(RBF_ERR_INVALID_ARGUMENT, "NULL peer pointer");
+    a.route.bufs[r] = dy_buffers[r];
+    a.flags[r] = flag_arrays[r];
+  }
+  a.route.world = world;
+  a.route.rank = rank;
+  a.route.ctr = step_counter;
+  a.ctr = step_counter;
+  a.tickets = tickets;
+  a.status = ws_at<int>(workspace, prep_layout(0, 0, 0).status);
+  a.timeout_ns = wait_config_from_env().timeout_ns;
+  return cuda_status(launch_dy_exchange(a, reinterpret_cast<cudaStream_t>(stream)),
+                     "exchange launch");
 }
 
 int rbf_sm100_read_status(void* workspace, rbf_stream_t stream, int* device_status) {

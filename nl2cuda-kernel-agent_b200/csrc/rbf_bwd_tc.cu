@@ -92,6 +92,7 @@ struct BwdArgs {
   int group;             // neighbouring j-blocks walked together (divides tiles_j and the grid)
   int64_t static_rows;   // group rows [0, static_rows) are split into contiguous per-CTA ranges;
   int* counter;          // tiles from static_rows * group on are claimed from this counter
+  DyRoute route;  // world > 0: dY partials go to this rank's slot of the routed buffers
   int ablate;     // development builds only (RBF_TRACE): 1 skip dX reduce, 2 skip rowsum add,
                   // 4 C-warps skip W^T, 8 R-warps skip W, 16 no MMAs, 32 skip dY flush
 };
@@ -574,6 +575,16 @@ __global__ void __launch_bounds__(THREADS, 1)
     float colsum = 0.f;
     TileCoord cur = {-1, -1, -1};
     bool ok = true;
+    // This step's slot of the routed dY buffer (fixed for the launch), picked with constant
+    // indices so that the pointer array stays out of local memory.
+    float* route_dst = nullptr;
+    if (a.route.world > 0) {
+      route_dst = a.route.bufs[0];
+#pragma unroll
+      for (int r = 1; r < kMaxRanks; ++r)
+        if (a.route.rank == r) route_dst = a.route.bufs[r];
+      route_dst += (int64_t)((*a.route.ctr) % kDySlots) * a.M * a.D;
+    }
     // Byte offset of this lane's column inside a 128-byte swizzled row, for row % 8 = r.
     uint32_t coff[8];
 #pragma unroll
@@ -641,7 +652,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #ifdef RBF_TRACE
         if (a.ablate & 32) continue;
 #endif
-        if (j < a.M) flush_row<DS>(a.dY, a.Y, j, a.D, tc.slice * DS, a.c, colsum, accv);
+        float* dst = a.route.world > 0 ? route_dst : a.dY;
+        if (j < a.M) flush_row<DS>(dst, a.Y, j, a.D, tc.slice * DS, a.c, colsum, accv);
         if (lane == 0 && q == 0) TRACE(4, 50);
       }
     }
@@ -808,9 +820,12 @@ __global__ void __launch_bounds__(256) rbf_bwd_finalize_kernel(const float* __re
 // launch, so the stream stays a chain of kernels that programmatic dependent launch can overlap.
 __global__ void __launch_bounds__(256) rbf_bwd_zero_kernel(float* __restrict__ a, int64_t na,
                                                            float* __restrict__ b, int64_t nb,
-                                                           float* __restrict__ c, int64_t nc) {
+                                                           float* __restrict__ c, int64_t nc,
+                                                           const int* __restrict__ slot_ctr) {
   ptx::griddep_wait();
   ptx::griddep_launch_dependents();
+  // Routed dY: b is slot 0 of this rank's buffer and the step counter picks the slot.
+  if (slot_ctr != nullptr) b += (int64_t)(*slot_ctr % kDySlots) * nb;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < na + nb + nc; k += stride) {
     if (k < na) a[k] = 0.f;
@@ -836,8 +851,10 @@ bool backward_tc_supported(int64_t N, int64_t M, int64_t D) {
 
 cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, const float* K,
                                float* dX, float* dY, int64_t N, int64_t M, int64_t D,
-                               float gamma, void* ws, const WaitConfig& wc, cudaStream_t stream) {
+                               float gamma, void* ws, const WaitConfig& wc, cudaStream_t stream,
+                               const DyRoute* route) {
   cudaError_t e;
+  const bool routed = route != nullptr && route->world > 0;
   const PrepLayout L = prep_layout(N, M, D);
   const bool tma_flush = (D % 4) == 0;  // dX rows 16-byte pitched
   float* rowsum = ws_at<float>(ws, L.end);
@@ -847,11 +864,19 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
     // rowsum and the counter are adjacent: one range covers both (or just the counter).
     float* zc = (work && tma_flush) ? rowsum : reinterpret_cast<float*>(counter);
     const int64_t nz = (work && tma_flush) ? rowsum_bytes(N) / 4 + 1 : (work ? 1 : 0);
-    const int64_t total = N * D + M * D + nz;
+    // Routed: this rank's slot of the dY buffer instead of the caller's dY.
+    float* zy = dY;
+    const int* zctr = nullptr;
+    if (routed) {
+      zy = route->bufs[route->rank];
+      zctr = route->ctr;
+    }
+    const int64_t ny = M * D;
+    const int64_t total = N * D + ny + nz;
     if (total > 0) {
       const int64_t blocks = std::min<int64_t>(ceil_div(total, 256), 4 * device_sm_count());
       if ((e = launch_kernel(rbf_bwd_zero_kernel, dim3((unsigned)blocks), dim3(256), 0, stream, dX,
-                             N * D, dY, M * D, zc, nz)) != cudaSuccess)
+                             N * D, zy, ny, zc, nz, zctr)) != cudaSuccess)
         return e;
       note_launches(1);
     }
@@ -886,6 +911,8 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
   a.num_slices = (int)ceil_div(L.Dp, DS);
   a.total_tiles = (int64_t)a.tiles_i * a.tiles_j * a.num_slices;
   a.counter = counter;
+  a.route = routed ? *route : DyRoute{};
+  if (!routed) a.route.world = 0;
   const int grid = (int)std::min<int64_t>(a.total_tiles, device_sm_count());
   {
     // Group width (RBF_BWD_GROUP, default 4) and the share of tiles handed out dynamically

@@ -63,6 +63,18 @@ struct WaitConfig {
 };
 WaitConfig wait_config_from_env();
 
+// Row-sharded dY reduction without a library collective: every rank's backward accumulates its
+// dY partial into slot (*ctr % kDySlots) of its own buffer bufs[rank] (peer-visible memory, e.g.
+// CUDA symmetric memory; bufs[r] is rank r's buffer mapped in this process), and the exchange
+// kernel (rbf_exchange.cu) reduces and gathers over NVLink.  world == 0: the caller's dY.
+constexpr int kMaxRanks = 8;
+constexpr int kDySlots = 2;
+struct DyRoute {
+  float* bufs[kMaxRanks];
+  const int* ctr;
+  int world, rank;
+};
+
 // rbf_fwd_tc.cu: the tcgen05 3xTF32 forward (workspace must hold the split pass output).
 cudaError_t launch_forward_tc(const float* X, const float* Y, float* K, int64_t N, int64_t M,
                               int64_t D, float gamma, void* ws, const WaitConfig& wc,
@@ -85,7 +97,23 @@ bool backward_tc_supported(int64_t N, int64_t M, int64_t D);
 size_t backward_scratch_bytes(int64_t N, int64_t M, int64_t D);
 cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, const float* K,
                                float* dX, float* dY, int64_t N, int64_t M, int64_t D,
-                               float gamma, void* ws, const WaitConfig& wc, cudaStream_t stream);
+                               float gamma, void* ws, const WaitConfig& wc, cudaStream_t stream,
+                               const DyRoute* route = nullptr);
+
+// rbf_exchange.cu: completes a routed step -- barrier, owners reduce their j-blocks over every
+// rank's slot, barrier, every rank gathers dY from the owners, the step counter advances.
+// flags[r] is rank r's int[world] signal array (peer memory).
+struct ExchangeArgs {
+  float* dY;
+  int64_t M, D;
+  DyRoute route;
+  int* flags[kMaxRanks];
+  int* ctr;
+  unsigned* tickets;  // two zeroed counters, reused across steps
+  int* status;
+  unsigned long long timeout_ns;
+};
+cudaError_t launch_dy_exchange(const ExchangeArgs& a, cudaStream_t stream);
 
 // rbf_simt.cu: fp32 CUDA-core kernels (bring-up path).
 cudaError_t launch_forward_simt(const float* X, const float* Y, float* K, int64_t N, int64_t M,
