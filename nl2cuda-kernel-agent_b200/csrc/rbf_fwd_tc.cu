@@ -14,7 +14,7 @@
 //   warp 1    MMA issuer (one thread): 3 x tcgen05.mma.kind::tf32 (M=128, N=128, K=8) per 8
 //             features into one of two TMEM accumulators (2 x 128 columns), so the epilogue of
 //             tile t overlaps the MMAs of tile t+1.
-//   warps 2-9 epilogue: warp w reads TMEM lanes 32*(w%4).. (its row quadrant) and one half of
+//   warps 2.. epilogue: warp w reads TMEM lanes 32*(w%4).. (its row quadrant) and one column group of
 //             the columns, adds the norms, clamps, exponentiates (MUFU ex2), stages 32x32 fp32
 //             blocks in swizzled shared memory (two per warp, so a chunk never waits for the
 //             previous store to drain) and writes them with TMA stores (no multicast).
@@ -37,12 +37,21 @@ namespace {
 constexpr int BM = 128;
 constexpr int BN = 128;
 constexpr int BK = 32;
-constexpr int STAGES = 3;
-constexpr int EPI_WARPS = 8;
+#ifndef RBF_EPI_BUFS
+#define RBF_EPI_BUFS 1
+#endif
+#ifndef RBF_EPI_WARPS
+#define RBF_EPI_WARPS 8
+#endif
+constexpr int STAGES = (RBF_EPI_BUFS == 1 && RBF_EPI_WARPS == 8) ? 3 : 2;
+// Epilogue warps: 4 per TMEM lane quadrant, each converting one 32-column chunk per tile (more
+// warps per scheduler hide the latency of the exp (MUFU) and shuffle chains).
+constexpr int EPI_WARPS = RBF_EPI_WARPS;
+constexpr int CPW = 16 / EPI_WARPS;  // 32-column chunks per epilogue warp per tile
 constexpr int THREADS = 32 * (2 + EPI_WARPS);
 constexpr uint32_t TILE_BYTES = 128 * BK * 4;  // 16 KiB: 128 rows x 128 bytes
 constexpr uint32_t STAGE_BYTES = 4 * TILE_BYTES;
-constexpr int EPI_BUFS = 1;                                 // 32x32 fp32 staging blocks per warp
+constexpr int EPI_BUFS = RBF_EPI_BUFS;                      // 32x32 fp32 staging blocks per warp
 constexpr uint32_t EPI_BYTES = EPI_BUFS * 32 * 32 * 4;
 constexpr uint32_t TMEM_COLS = 2 * BN;
 constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + EPI_WARPS * EPI_BYTES + 256;
@@ -50,11 +59,11 @@ static_assert(SMEM_BYTES <= 232448, "forward shared memory over the sm_100 limit
 // Resident-X variant (D <= 64, at most two 32-feature chunks): the CTA walks its tiles along j,
 // so the X hi/lo slices of one row block stay in shared memory and only Y is streamed.
 constexpr int RA_CHUNKS = 2;
-constexpr int RB_STAGES = 4;
+constexpr int RB_STAGES = (EPI_BUFS == 1 && EPI_WARPS == 8) ? 4 : 3;
 constexpr uint32_t CHUNK_BYTES = 2 * TILE_BYTES;  // hi + lo of one 32-feature slice, 128 rows
 // Pair variant (two-CTA clusters, tcgen05.mma.cta_group::2, M = 256): each CTA keeps its own 128
 // X rows resident and streams only 64 of the tile's 128 Y rows, so Y traffic per SM halves.
-constexpr int PB_STAGES = 8;
+constexpr int PB_STAGES = 2 * RB_STAGES;  // the same bytes as the single-CTA Y ring
 constexpr uint32_t PCHUNK_BYTES = CHUNK_BYTES / 2;  // hi + lo of one slice, 64 rows
 constexpr int PAIR_ROWS = 64;
 constexpr size_t SMEM_BYTES_RA =
@@ -76,6 +85,20 @@ struct FwdArgs {
 
 #ifdef RBF_TRACE
 __device__ unsigned long long g_fwd_span[1024][3];
+// Development timeline of CTA 0 (trace builds only): per role, (code << 56 | globaltimer).
+__device__ unsigned long long g_ftrace[4][512];
+__device__ int g_ftrace_n[4];
+__device__ __forceinline__ void ftrace(int role, int code) {
+  if (blockIdx.x != 0) return;
+  const int n = g_ftrace_n[role];
+  if (n < 512) {
+    g_ftrace[role][n] = ((unsigned long long)code << 56) | (ptx::globaltimer() & ((1ull << 56) - 1));
+    g_ftrace_n[role] = n + 1;
+  }
+}
+#define FTRACE(role, code) ftrace(role, code)
+#else
+#define FTRACE(role, code) ((void)0)
 #endif
 
 template <bool TMA_STORE, bool RES_A, bool PAIR>
@@ -197,6 +220,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int kc = 0; kc < a.num_kc; ++kc) {
           if (!ptx::mbar_wait_bounded(&empty[stage], phase ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
+          FTRACE(0, 10 + kc);
           if (a.debug_skip_first_load && !skipped && blockIdx.x == 0) {
             skipped = true;  // test hook: this stage never fills, so its consumer times out
           } else {
@@ -293,6 +317,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           ok = false;
           break;
         }
+        FTRACE(1, 10);
         ptx::tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(acc * BN);
         for (int kc = 0; kc < a.num_kc; ++kc) {
@@ -336,6 +361,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (!ok) break;
         commit(&acc_full[acc]);
+        FTRACE(1, 20);
         // Last tile of this row block: the resident X may be replaced once these MMAs finish.
         if (RES_A && (t + 1 == t_end || (int)((t + 1) / a.tiles_n) != ib)) commit(a_empty);
         if (++acc == 2) {
@@ -350,61 +376,59 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;              // TMEM lane quadrant this warp may access
-    const int h = (warp - 2) >> 2;       // column half of the tile
+    const int h = (warp - 2) >> 2;       // column group of the tile (32 * CPW columns)
     uint8_t* buf = epi_mem + (warp - 2) * EPI_BYTES;
     int acc = 0;
     uint32_t acc_phase = 0;
-    // The norms of the next chunk are loaded one chunk ahead (and across tiles), so their
-    // global-load latency overlaps the accumulator wait and the previous chunk's math.
-    auto load_yn = [&](int64_t t, int c, float (&dst)[32]) {
-      const int64_t j = (t % a.tiles_n) * BN + h * 64 + c * 32;
-      if (j + 32 <= a.M) {
-        const float4* y4 = reinterpret_cast<const float4*>(a.yn + j);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float4 f = __ldg(y4 + e);
-          dst[4 * e] = f.x; dst[4 * e + 1] = f.y; dst[4 * e + 2] = f.z; dst[4 * e + 3] = f.w;
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) dst[e] = (j + e < a.M) ? __ldg(a.yn + j + e) : 0.f;
-      }
+    // The norms of the next tile are loaded one whole tile ahead (the first touch of a column
+    // block after an L2 flush misses to DRAM): each lane holds ||y||^2 of its own column in the
+    // two 32-column chunks and the chunk's 32 values are broadcast with warp shuffles.
+    auto load_yn = [&](int64_t t, int c) {
+      const int64_t j = (t % a.tiles_n) * BN + h * (32 * CPW) + c * 32 + lane;
+      return j < a.M ? __ldg(a.yn + j) : 0.f;
     };
     auto load_xn = [&](int64_t t) {
       const int64_t i = (t / a.tiles_n) * TILE_ROWS + rank * BM + q * 32 + lane;
       return i < a.N ? __ldg(a.xn + i) : 0.f;
     };
-    float ynext[32];
-    float xnext = 0.f;
+    float xnext = 0.f, ynext[CPW];
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) ynext[c] = 0.f;
     if (t_begin < t_end) {
-      load_yn(t_begin, 0, ynext);
       xnext = load_xn(t_begin);
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) ynext[c] = load_yn(t_begin, c);
     }
     for (int64_t t = t_begin; t < t_end; ++t) {
       const int64_t i0 = (t / a.tiles_n) * TILE_ROWS + rank * BM;
       const int64_t j0 = (t % a.tiles_n) * BN;
       if (!ptx::mbar_wait_bounded(&acc_full[acc], acc_phase, a.status, a.timeout_ns)) break;
+      if (lane == 0 && (warp == 2 || warp == 9)) FTRACE(warp == 2 ? 2 : 3, 30);
       ptx::tc_fence_after();
       const int64_t i = i0 + q * 32 + lane;
       const float xi = xnext;
-      if (t + 1 < t_end) xnext = load_xn(t + 1);
+      float ylane[CPW];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int col0 = h * 64 + c * 32;
-        float yv[32];
+      for (int c = 0; c < CPW; ++c) ylane[c] = ynext[c];
+      if (t + 1 < t_end) {
+        xnext = load_xn(t + 1);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) yv[e] = ynext[e];
-        if (c == 0) load_yn(t, 1, ynext);
-        else if (t + 1 < t_end) load_yn(t + 1, 0, ynext);
+        for (int c = 0; c < CPW; ++c) ynext[c] = load_yn(t + 1, c);
+      }
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) {
+        const int col0 = h * (32 * CPW) + c * 32;
         uint32_t v[32];
         ptx::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + col0), v);
         ptx::tmem_wait_ld();
-        if (c == 1) {
+        if (lane == 0 && warp == 2) FTRACE(2, 60 + c);
+        if (c == CPW - 1) {
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) {
             if (PAIR) ptx::mbar_arrive_cluster(ptx::map_to_rank(&acc_empty[acc], 0));
             else ptx::mbar_arrive(&acc_empty[acc]);
+            if (warp == 2 || warp == 9) FTRACE(warp == 2 ? 2 : 3, 50);
           }
         }
         const int64_t j = j0 + col0;
@@ -414,16 +438,28 @@ __global__ void __launch_bounds__(THREADS, 1)
         float out[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          const float d2 = fmaxf(fmaf(-2.f, __uint_as_float(v[e]), xi + yv[e]), 0.f);
+          const float yj = __shfl_sync(0xffffffffu, ylane[c], e);
+          const float d2 = fmaxf(fmaf(-2.f, __uint_as_float(v[e]), xi + yj), 0.f);
           out[e] = exp2_approx(d2 * a.scale);
         }
 #ifdef RBF_TRACE
+        if (lane == 0 && warp == 2) FTRACE(2, 70 + c);
         if (a.ablate == 3) { if (out[lane] == 12345.f) a.K[0] = 1.f; continue; }
+#endif
+#ifdef RBF_FWD_DIRECT
+        if (TMA_STORE && i < a.N) {
+          float4* krow = reinterpret_cast<float4*>(a.K + i * a.M + j);
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4)
+            krow[c4] = make_float4(out[4 * c4], out[4 * c4 + 1], out[4 * c4 + 2], out[4 * c4 + 3]);
+          if (warp == 2 || warp == 9) FTRACE(warp == 2 ? 2 : 3, 40 + c);
+        } else
 #endif
         if (TMA_STORE) {
           // EPI_BUFS staging blocks per warp, reused once the store that last read them is done.
           uint8_t* blk = buf + (c % EPI_BUFS) * (32 * 32 * 4);
           if (lane == 0) ptx::bulk_wait_read<EPI_BUFS - 1>();
+          if (lane == 0 && warp == 2) FTRACE(2, 80 + c);
           __syncwarp();
           uint8_t* row = blk + lane * 128;
 #pragma unroll
@@ -435,6 +471,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           __syncwarp();
           if (lane == 0) {
             ptx::tma_store_2d(&tm_k, blk, (int32_t)j, (int32_t)(i0 + q * 32));
+            if (warp == 2 || warp == 9) FTRACE(warp == 2 ? 2 : 3, 40 + c);
             ptx::bulk_commit();
           }
         } else if (i < a.N) {
@@ -639,5 +676,15 @@ extern "C" __attribute__((visibility("default"))) int rbf_debug_fwd_spans(unsign
 extern "C" __attribute__((visibility("default"))) int rbf_debug_fwd_spans_clear() {
   static unsigned long long z[1024][3];
   return (int)cudaMemcpyToSymbol(rbf::g_fwd_span, z, sizeof(z));
+}
+#endif
+
+#ifdef RBF_TRACE
+extern "C" __attribute__((visibility("default"))) int rbf_debug_fwd_trace(unsigned long long* out,
+                                                                          int* n) {
+  cudaMemcpyFromSymbol(out, rbf::g_ftrace, sizeof(rbf::g_ftrace));
+  cudaMemcpyFromSymbol(n, rbf::g_ftrace_n, sizeof(rbf::g_ftrace_n));
+  int z[4] = {0, 0, 0, 0};
+  return (int)cudaMemcpyToSymbol(rbf::g_ftrace_n, z, sizeof(z));
 }
 #endif
