@@ -392,7 +392,10 @@ def main():
 def run_e2e(X, Y, G, g, world, dev, args, shard, op, route=None):
     """Same metric through the public API, host buffers in and out: per step the H2D copy of
     X (this rank's rows), Y and G from pinned memory, forward + backward, and the D2H copy of
-    K, dX and dY into pinned memory, all inside the events."""
+    K, dX and dY into pinned memory, all inside the events.  On one GPU the copies overlap the
+    compute the way a user would pipeline them: G (needed only by the backward) is copied on a
+    side stream during the forward, and K is copied back on another side stream during the
+    backward (H2D and D2H use separate copy engines)."""
     import torch
     Xh = X.cpu().pin_memory()
     Yh = Y.cpu().pin_memory()
@@ -403,22 +406,36 @@ def run_e2e(X, Y, G, g, world, dev, args, shard, op, route=None):
     dXh = torch.empty(n, D, dtype=torch.float32).pin_memory()
     dYh = torch.empty(M, D, dtype=torch.float32).pin_memory()
     stream = torch.cuda.current_stream(dev)
+    h2d = torch.cuda.Stream(device=dev)
+    d2h = torch.cuda.Stream(device=dev)
 
     def one():
         Xd = Xh.to(dev, non_blocking=True)
         Yd = Yh.to(dev, non_blocking=True)
-        Gd = Gh.to(dev, non_blocking=True)
         if world == 1:
+            h2d.wait_stream(stream)  # inside the step's timed region
+            with torch.cuda.stream(h2d):
+                Gd = Gh.to(dev, non_blocking=True)
+            Gd.record_stream(stream)
             Xd.requires_grad_(True)
             Yd.requires_grad_(True)
             K = op.candidate({"X": Xd, "Y": Yd}, {"gamma": g})
+            d2h.wait_stream(stream)  # K is complete
+            with torch.cuda.stream(d2h):
+                Kh.copy_(K.detach(), non_blocking=True)
+            K.record_stream(d2h)
+            stream.wait_stream(h2d)  # G has arrived
             K.backward(Gd)
             dX, dY = Xd.grad, Yd.grad
+            dXh.copy_(dX, non_blocking=True)
+            dYh.copy_(dY, non_blocking=True)
+            stream.wait_stream(d2h)  # the K copy is inside the timed region
         else:
+            Gd = Gh.to(dev, non_blocking=True)
             K, dX, dY = shard.forward_backward_shard(Xd, Yd, Gd, g, route=route)
-        Kh.copy_(K.detach(), non_blocking=True)
-        dXh.copy_(dX, non_blocking=True)
-        dYh.copy_(dY, non_blocking=True)
+            Kh.copy_(K.detach(), non_blocking=True)
+            dXh.copy_(dX, non_blocking=True)
+            dYh.copy_(dY, non_blocking=True)
 
     for _ in range(max(2, args.warmup)):
         one()

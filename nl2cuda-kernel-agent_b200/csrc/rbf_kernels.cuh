@@ -115,9 +115,7 @@ struct ExchangeArgs {
 };
 cudaError_t launch_dy_exchange(const ExchangeArgs& a, cudaStream_t stream);
 
-// rbf_simt.cu: fp32 CUDA-core kernels (bring-up path).
-cudaError_t launch_forward_simt(const float* X, const float* Y, float* K, int64_t N, int64_t M,
-                                int64_t D, float gamma, const void* ws, cudaStream_t stream);
+// rbf_simt.cu: fp32 CUDA-core backward for M % 4 != 0.
 cudaError_t launch_backward_simt(const float* X, const float* Y, const float* G, const float* K,
                                  float* dX, float* dY, int64_t N, int64_t M, int64_t D,
                                  float gamma, cudaStream_t stream);
