@@ -282,6 +282,12 @@ int rbf_sm100_dy_exchange(float* dY, int64_t M, int64_t D, float* const* dy_buff
   a.tickets = tickets;
   a.status = ws_at<int>(workspace, prep_layout(0, 0, 0).status);
   a.timeout_ns = wait_config_from_env().timeout_ns;
+  // Up to RBF_XCHG_ONE_PHASE_MAX ranks (default 8, i.e. always) every rank sums all partials
+  // after one barrier; beyond, owners reduce, then a second barrier and a gather.  At 8 ranks
+  // and c1 the one-phase read is ~7 MB per rank over NVLink (~9 us), about the cost of the
+  // second barrier the two-phase form needs (measured +8 us at 2 ranks).
+  a.one_phase_max = 8;
+  if (const char* s = std::getenv("RBF_XCHG_ONE_PHASE_MAX")) a.one_phase_max = std::atoi(s);
   return cuda_status(launch_dy_exchange(a, reinterpret_cast<cudaStream_t>(stream)),
                      "exchange launch");
 }

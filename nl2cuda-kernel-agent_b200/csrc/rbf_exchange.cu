@@ -7,9 +7,9 @@
 //   1. barrier A: store epoch 2*ctr + 1 into flags[r][rank] of every rank r (release, system
 //      scope), wait until this rank's flags[rank][r] >= 2*ctr + 1 for every r -- every partial
 //      is complete;
-//   up to 4 ranks:
+//   one-phase (default up to 8 ranks):
 //   2'. every rank sums slot s over all ranks (peer loads) straight into its dY;
-//   more ranks (less NVLink traffic per rank, one more barrier):
+//   two-phase (less NVLink traffic per rank, one more barrier):
 //   2. for the 128-row j-blocks this rank owns (jb % world == rank), sum slot s over all ranks
 //      and write the sum back into this rank's slot, in place;
 //   3. barrier B (epoch 2*ctr + 2), released by the last block to finish step 2;
@@ -33,7 +33,6 @@ namespace {
 constexpr int kBlockRows = 128;  // j-block height of the backward's tiles (dY ownership unit)
 constexpr int kThreads = 256;
 constexpr int kChunkRows = 16;        // unit of work: 16 rows of dY (one float4 per thread at D = 64)
-constexpr int kOnePhaseMaxRanks = 4;  // up to 4 ranks every rank sums all partials (one barrier)
 
 #ifdef RBF_TRACE
 __device__ unsigned long long g_xchg_trace[8];
@@ -122,7 +121,7 @@ __global__ void __launch_bounds__(kThreads) rbf_dy_exchange_kernel(const Exchang
   const int64_t slot = (int64_t)(ctr % kDySlots) * a.M * a.D;
   const int64_t chunks = (a.M + kChunkRows - 1) / kChunkRows;
   const int per_block = kBlockRows / kChunkRows;  // chunks per 128-row j-block
-  const bool two_phase = world > kOnePhaseMaxRanks;
+  const bool two_phase = world > a.one_phase_max;
 
   // 1. Barrier A: every rank's partial is complete.
   if (threadIdx.x == 0) {

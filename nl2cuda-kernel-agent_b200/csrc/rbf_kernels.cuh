@@ -110,6 +110,7 @@ struct ExchangeArgs {
   int* flags[kMaxRanks];
   int* ctr;
   unsigned* tickets;  // two zeroed counters, reused across steps
+  int one_phase_max;  // up to this many ranks: one barrier, every rank sums all partials
   int* status;
   unsigned long long timeout_ns;
 };

@@ -28,14 +28,15 @@ def _inputs():
     return X, Y, G
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, one_phase_max):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     for p in (os.path.join(root, "nl2cuda-kernel-agent_b200"), root):
         sys.path.insert(0, p)
     import torch.distributed as dist
     from cases.rbf import native, shard
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      RBF_XCHG_ONE_PHASE_MAX=str(one_phase_max))
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
@@ -89,11 +90,14 @@ def _worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def test_two_gpu_routed_dy(tmp_path):
+@pytest.mark.parametrize("one_phase_max", [8, 0])
+def test_two_gpu_routed_dy(tmp_path, one_phase_max):
+    """one_phase_max 8: one barrier, every rank sums all partials (the default);
+    0: owners reduce, second barrier, gather."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
-    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path), one_phase_max), nprocs=2, join=True)
     assert all((tmp_path / f"ok_{r}").exists() for r in range(2))
     from oracle import oracle
     X, Y, G = _inputs()
