@@ -415,22 +415,25 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int c = 0; c < CPW; ++c) ynext[c] = load_yn(t + 1, c);
       }
+      // All of this warp's accumulator columns are read at once (one TMEM round trip) and the
+      // accumulator goes back to the MMA issuer before the math.
+      uint32_t vall[CPW][32];
+#pragma unroll
+      for (int c = 0; c < CPW; ++c)
+        ptx::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + h * (32 * CPW) + c * 32),
+                       vall[c]);
+      ptx::tmem_wait_ld();
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (PAIR) ptx::mbar_arrive_cluster(ptx::map_to_rank(&acc_empty[acc], 0));
+        else ptx::mbar_arrive(&acc_empty[acc]);
+        if (warp == 2 || warp == 9) FTRACE(warp == 2 ? 2 : 3, 50);
+      }
 #pragma unroll
       for (int c = 0; c < CPW; ++c) {
         const int col0 = h * (32 * CPW) + c * 32;
-        uint32_t v[32];
-        ptx::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + col0), v);
-        ptx::tmem_wait_ld();
-        if (lane == 0 && warp == 2) FTRACE(2, 60 + c);
-        if (c == CPW - 1) {
-          ptx::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            if (PAIR) ptx::mbar_arrive_cluster(ptx::map_to_rank(&acc_empty[acc], 0));
-            else ptx::mbar_arrive(&acc_empty[acc]);
-            if (warp == 2 || warp == 9) FTRACE(warp == 2 ? 2 : 3, 50);
-          }
-        }
+        const uint32_t (&v)[32] = vall[c];
         const int64_t j = j0 + col0;
 #ifdef RBF_TRACE
         if (a.ablate == 2 || a.ablate == 4) continue;
