@@ -11,8 +11,9 @@ gradient G, fp32 in and out.  FLOP per step = 6*N*M*D; algorithmic HBM bytes per
 N = 1 runs config c1 (N=M=4096, D=64).  Under torchrun (WORLD_SIZE = N > 1) the work is
 weak-scaled by rows: every rank owns 4096 rows of X (and of G, K), Y (4096 x 64) is replicated,
 and the partial dY is reduced inside the backward over NVLink peer memory (the dY partials go
-straight into the owning rank's buffer, then one bounded cross-GPU barrier and a gather;
-RBF_DY_REDUCE=nccl uses one NCCL all-reduce instead) ("scaling": "weak").
+straight into the owning rank's buffer, then one bounded cross-GPU barrier and a gather) up to 4
+ranks, and with one NCCL all-reduce beyond, where that measured faster (RBF_DY_REDUCE=peer or
+nccl forces either) ("scaling": "weak").
 ``value`` = whole-job GFLOP/s = (6 * N_global * M * D) / (max over ranks of the device time of
 one step).  Inputs are resident in HBM when timing starts; L2 is flushed (256 MiB write) before
 every timed step, outside the events.
@@ -249,7 +250,12 @@ def main():
     route = None
     dy_reduce = "none"
     if world > 1:
-        dy_reduce = os.environ.get("RBF_DY_REDUCE", "peer")
+        # auto: the library's NVLink peer exchange up to 4 ranks, where it measured faster than
+        # NCCL (109.5 vs 115.5 us per step at 2 GPUs, 115.7 vs 119.2 at 4); NCCL at 8 (129.5 vs
+        # 133.5 us: every rank then reads 7 MB of partials).
+        dy_reduce = os.environ.get("RBF_DY_REDUCE", "auto")
+        if dy_reduce == "auto":
+            dy_reduce = "peer" if world <= 4 else "nccl"
         if dy_reduce == "peer":
             route = shard.RoutedDy(M, D, dev)
 
