@@ -30,6 +30,9 @@ SHAPES = [
     (200, 300, 64, 1 / 64), (129, 260, 32, 0.5 / 32), (513, 1028, 64, 1 / 64), (4, 8, 3, 0.3),
     (1, 4, 1, 0.5), (700, 516, 256, 1 / 256), (300, 400, 100, 0.01), (1100, 1200, 128, 1 / 128),
     (77, 4096, 64, 1 / 64), (4096, 36, 48, 0.02),
+    # M % 4 == 0 with D % 4 != 0: tensor-core backward, dX flushed with red.add; D = 130 runs two
+    # 64-feature slices (G and K read twice)
+    (517, 1000, 37, 1 / 37), (300, 400, 130, 1 / 130),
 ]
 
 
