@@ -1,0 +1,54 @@
+"""framework/profile.py: the ncu CSV summaries (hand-made fixtures in ncu's CSV shape) and the
+capture commands; no GPU needed."""
+import os
+
+import pytest
+
+from framework import profile
+
+FIX = os.path.join(os.path.dirname(os.path.abspath(__file__)), "fixtures")
+
+
+def _read(name):
+    with open(os.path.join(FIX, name)) as f:
+        return f.read()
+
+
+def test_launch_list_summary():
+    s = profile.summarize_launches(_read("ncu_launches_sample.csv"))
+    assert [k for k, *_ in s] == ["kern_b(float *)", "kern_a(int)"]
+    (kb, nb, tb, mb, shb), (ka, na, ta, ma, sha) = s
+    assert (nb, na) == (1, 2)
+    assert tb == pytest.approx(9.0) and ta == pytest.approx(8.0) and ma == pytest.approx(4.0)
+    assert shb + sha == pytest.approx(1.0)
+    assert "kern_a(int)" in profile.format_launches(s)
+
+
+def test_raw_summary_units_and_stalls():
+    (r,) = profile.summarize_raw(_read("ncu_raw_sample.csv"))
+    assert r["duration_us"] == pytest.approx(12.5)
+    assert r["dram_read"] == pytest.approx(100.5e6) and r["dram_write"] == pytest.approx(512e3)
+    assert r["tensor_pct"] == pytest.approx(17.25)
+    assert r["stalls"][0] == ("long_scoreboard", 3.5)
+    text = profile.format_raw([r])
+    assert "traffic 101.01 MB" in text and "long_scoreboard 3.50" in text
+
+
+def test_ncu_commands_keep_clock_control_none():
+    cmds = profile.ncu_commands("rbf", None)
+    assert all("--clock-control none" in c for c in cmds if c.startswith("python"))
+    assert any("--page raw --csv" in c for c in cmds)
+
+
+def test_cli_summaries(capsys):
+    assert profile.main(["--launches", os.path.join(FIX, "ncu_launches_sample.csv")]) == 0
+    assert "kern_b" in capsys.readouterr().out
+    assert profile.main(["--raw", os.path.join(FIX, "ncu_raw_sample.csv")]) == 0
+    assert "tensor pipe %" in capsys.readouterr().out
+
+
+@pytest.mark.gpu
+def test_profile_candidate_sees_the_library_kernels(cuda_device):
+    table, cuda_us, wall_us = profile.profile_candidate("rbf", mode="both", iters=3)
+    assert "rbf_fwd_tc_kernel" in table and "rbf_bwd_tc_kernel" in table
+    assert 0 < cuda_us and 0 < wall_us
