@@ -13,7 +13,9 @@
 //             Yhi, Ylo (128 rows each), 128-byte swizzled, into a 2-deep ring (64 KiB/stage).
 //   warp 1    MMA issuer (one thread): 3 x tcgen05.mma.kind::tf32 (M=128, N=128, K=8) per 8
 //             features into one of two TMEM accumulators (2 x 128 columns), so the epilogue of
-//             tile t overlaps the MMAs of tile t+1.
+//             tile t overlaps the MMAs of tile t+1.  With X resident (D <= 64) the thread
+//             copies X hi|lo from shared memory into TMEM (tcgen05.cp, columns 256..383) once
+//             per row block and the MMAs take A from TMEM, so only Y is read from shared memory.
 //   warps 2.. epilogue: warp w reads TMEM lanes 32*(w%4).. (its row quadrant) and one column group of
 //             the columns, adds the norms, clamps, exponentiates (MUFU ex2), stages 32x32 fp32
 //             blocks in swizzled shared memory (two per warp, so a chunk never waits for the
@@ -54,6 +56,13 @@ constexpr uint32_t STAGE_BYTES = 4 * TILE_BYTES;
 constexpr int EPI_BUFS = RBF_EPI_BUFS;                      // 32x32 fp32 staging blocks per warp
 constexpr uint32_t EPI_BYTES = EPI_BUFS * 32 * 32 * 4;
 constexpr uint32_t TMEM_COLS = 2 * BN;
+// X-in-TMEM variant (resident X, single CTA): the MMA's A operand (X hi | X lo, 64 columns each)
+// sits in TMEM after the two accumulators, so the MMAs read only Y from shared memory.
+#ifndef RBF_FWD_ATMEM
+#define RBF_FWD_ATMEM 1
+#endif
+constexpr uint32_t XCOL = 2 * BN;
+constexpr uint32_t TMEM_COLS_AT = 512;
 constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + EPI_WARPS * EPI_BYTES + 256;
 static_assert(SMEM_BYTES <= 232448, "forward shared memory over the sm_100 limit");
 // Resident-X variant (D <= 64, at most two 32-feature chunks): the CTA walks its tiles along j,
@@ -134,6 +143,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   // CTAs' operand bytes (full, a_full) and both CTAs' epilogue releases (acc_empty).
   const uint32_t rank = PAIR ? ptx::cluster_ctarank() : 0;
   const bool leader = rank == 0;
+  constexpr bool A_TMEM = RES_A && !PAIR && RBF_FWD_ATMEM;
+  constexpr uint32_t TCOLS = A_TMEM ? TMEM_COLS_AT : TMEM_COLS;
   if (threadIdx.x == 0) {
     for (int s = 0; s < 8; ++s) {
       ptx::mbar_init(&full[s], 1);
@@ -158,10 +169,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (PAIR) ptx::cluster_sync();  // the peer's barriers exist before any remote arrive
   if (warp == 1) {
     if (PAIR) {
-      ptx::tmem_alloc_pair(tmem_slot, TMEM_COLS);
+      ptx::tmem_alloc_pair(tmem_slot, TCOLS);
       ptx::tmem_relinquish_pair();
     } else {
-      ptx::tmem_alloc(tmem_slot, TMEM_COLS);
+      ptx::tmem_alloc(tmem_slot, TCOLS);
       ptx::tmem_relinquish();
     }
   }
@@ -310,8 +321,23 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int ib = (int)(t / a.tiles_n);
         if (RES_A && ib != cur_ib) {
           cur_ib = ib;
+          // X in TMEM: the previous row block's MMAs must be done before its X is overwritten.
+          if (A_TMEM && !ptx::mbar_wait_bounded(a_empty, a_phase ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
           if (!ptx::mbar_wait_bounded(a_full, a_phase, a.status, a.timeout_ns)) { ok = false; break; }
           a_phase ^= 1;
+          if (A_TMEM) {
+            ptx::tc_fence_after();
+            for (int kc = 0; kc < a.num_kc; ++kc) {
+              const uint32_t xb = ptx::smem_u32(stage_mem + kc * CHUNK_BYTES);
+#pragma unroll
+              for (int k = 0; k < BK / 8; ++k) {
+                const uint32_t col = (uint32_t)(kc * (BK / 8) + k) * 8;
+                ptx::tmem_cp_128x256b(tmem + XCOL + col, ptx::smem_desc(xb + 32 * k, 16, 1024, 2));
+                ptx::tmem_cp_128x256b(tmem + XCOL + 64 + col,
+                                      ptx::smem_desc(xb + TILE_BYTES + 32 * k, 16, 1024, 2));
+              }
+            }
+          }
         }
         if (!ptx::mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1, a.status, a.timeout_ns)) {
           ok = false;
@@ -343,7 +369,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 #ifdef RBF_TRACE
             if (a.ablate == 1 || a.ablate == 4) continue;
 #endif
-            if (PAIR) {
+            if (A_TMEM) {
+              const uint32_t xa = tmem + XCOL + (uint32_t)(kc * (BK / 8) + k) * 8;
+              ptx::mma_tf32_ts(d, xa, bhi, idesc, (kc | k) != 0);
+              ptx::mma_tf32_ts(d, xa, blo, idesc, 1);
+              ptx::mma_tf32_ts(d, xa + 64, bhi, idesc, 1);
+            } else if (PAIR) {
               ptx::mma_tf32_ss_pair(d, ahi, bhi, idesc, (kc | k) != 0);
               ptx::mma_tf32_ss_pair(d, ahi, blo, idesc, 1);
               ptx::mma_tf32_ss_pair(d, alo, bhi, idesc, 1);
@@ -503,8 +534,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #endif
   if (warp == 1) {
     ptx::tc_fence_after();
-    if (PAIR) ptx::tmem_dealloc_pair(tmem, TMEM_COLS);
-    else ptx::tmem_dealloc(tmem, TMEM_COLS);
+    if (PAIR) ptx::tmem_dealloc_pair(tmem, TCOLS);
+    else ptx::tmem_dealloc(tmem, TCOLS);
   }
 }
 

@@ -305,6 +305,13 @@ __device__ __forceinline__ void mma_commit_pair(uint64_t* bar) {
       : "memory");
 }
 
+// Copy a 128-row x 256-bit (8 x 32-bit) matrix from shared memory (an MMA-operand descriptor)
+// into TMEM lanes 0..127, columns taddr.. taddr+7.  Asynchronous; ordered with the tcgen05.mma
+// operations this thread issues afterwards, and tracked by tcgen05.commit like them.
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
