@@ -82,19 +82,43 @@ def traffic_table():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    """SM clock and throttle reasons sampled while the timed region runs: through NVML every
+    ~2 ms (the timed region lasts milliseconds), else nvidia-smi every 200 ms.  Read-only."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event (throttle) reason bits
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40}
 
-    def __init__(self, gpu_id):
+    def __init__(self, gpu_id, period_s=0.002):
         self.gpu_id = gpu_id
+        self.period_s = period_s
         self.proc = None
         self.lines = []
         self.thread = None
+        self.nvml = None
+        self.samples = []  # (sm_mhz, reason bits) from NVML
+        self.max_mhz = None
+        self.running = False
 
     def start(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(int(self.gpu_id))
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
+            self.nvml = (pynvml, h, reasons)
+        except Exception:
+            self.nvml = None
+        if self.nvml is not None:
+            self.running = True
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu_id), f"--query-gpu={self.FIELDS}",
@@ -106,11 +130,32 @@ class ClockSampler:
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
 
+    def _poll(self):
+        pynvml, h, reasons = self.nvml
+        while self.running:
+            try:
+                self.samples.append((float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)),
+                                     int(reasons(h))))
+            except Exception:
+                return
+            time.sleep(self.period_s)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def stop(self):
+        if self.nvml is not None:
+            self.running = False
+            if self.thread:
+                self.thread.join(timeout=2)
+            if not self.samples:
+                return None
+            names = sorted(n for n, bit in self.REASON_BITS.items()
+                           if any(r & bit for _, r in self.samples))
+            return {"sm_mhz": statistics.median(s for s, _ in self.samples),
+                    "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples),
+                    "source": "nvml"}
         if self.proc is None:
             return None
         time.sleep(0.25)
@@ -138,7 +183,7 @@ class ClockSampler:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi"}
 
 
 def nvsmi_id(device):

@@ -194,7 +194,7 @@ def profile_candidate(case_name, impl=None, mode="both", iters=20, seed=0):
     for _ in range(3):
         once()
     torch.cuda.synchronize()
-    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA], acc_events=True) as prof:
         t0 = time.perf_counter()
         for _ in range(iters):
             once()
