@@ -107,7 +107,9 @@ class ClockSampler:
         try:
             import pynvml
             pynvml.nvmlInit()
-            h = pynvml.nvmlDeviceGetHandleByIndex(int(self.gpu_id))
+            gid = str(self.gpu_id)
+            h = (pynvml.nvmlDeviceGetHandleByUUID(gid) if gid.startswith("GPU-")
+                 else pynvml.nvmlDeviceGetHandleByIndex(int(gid)))
             self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
             reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
                 getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
