@@ -83,7 +83,7 @@ def traffic_table():
 
 class ClockSampler:
     """SM clock and throttle reasons sampled while the timed region runs: through NVML every
-    ~2 ms (the timed region lasts milliseconds), else nvidia-smi every 200 ms.  Read-only."""
+    ~0.5 ms (the timed region lasts milliseconds), else nvidia-smi every 200 ms.  Read-only."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -92,7 +92,7 @@ class ClockSampler:
     REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
                    "hw_thermal_slowdown": 0x40}
 
-    def __init__(self, gpu_id, period_s=0.002):
+    def __init__(self, gpu_id, period_s=0.0005):
         self.gpu_id = gpu_id
         self.period_s = period_s
         self.proc = None
@@ -118,6 +118,10 @@ class ClockSampler:
             self.nvml = None
         if self.nvml is not None:
             self.running = True
+            # The timed region lasts milliseconds: let the polling thread take the interpreter
+            # often enough (the default switch interval is 5 ms).
+            self.switch = sys.getswitchinterval()
+            sys.setswitchinterval(1e-4)
             self.thread = threading.Thread(target=self._poll, daemon=True)
             self.thread.start()
             return
@@ -151,6 +155,7 @@ class ClockSampler:
             self.running = False
             if self.thread:
                 self.thread.join(timeout=2)
+            sys.setswitchinterval(self.switch)
             if not self.samples:
                 return None
             names = sorted(n for n, bit in self.REASON_BITS.items()
