@@ -916,8 +916,8 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
   const int grid = (int)std::min<int64_t>(a.total_tiles, device_sm_count());
   {
     // Group width (RBF_BWD_GROUP, default 4) and the share of tiles handed out dynamically
-    // (RBF_BWD_DYN_PCT, default 30).
-    int group = 4, pct = 30;
+    // (RBF_BWD_DYN_PCT, default 15).
+    int group = 4, pct = 15;
     if (const char* s = std::getenv("RBF_BWD_GROUP")) group = std::max(1, std::atoi(s));
     if (const char* s = std::getenv("RBF_BWD_DYN_PCT")) pct = std::max(0, std::min(100, std::atoi(s)));
     if (a.tiles_j % group != 0 || grid % group != 0 || grid < group) group = 1;
