@@ -15,8 +15,9 @@ straight into the owning rank's buffer, then one bounded cross-GPU barrier and a
 ranks, and with one NCCL all-reduce beyond, where that measured faster (RBF_DY_REDUCE=peer or
 nccl forces either) ("scaling": "weak").
 ``value`` = whole-job GFLOP/s = (6 * N_global * M * D) / (max over ranks of the device time of
-one step).  Inputs are resident in HBM when timing starts; L2 is flushed (256 MiB write) before
-every timed step, outside the events.
+one step).  Inputs are resident in HBM when timing starts; L2 is flushed before every timed
+step, outside the events: a 256 MiB write, then a 256 MiB read of a second buffer, so that the
+flush's own dirty lines are written back before the step rather than during it.
 
 ``--impl reference`` times the reference's own CPU implementation of the path (its broadcast
 ``reference.py`` forward + torch autograd, restated in oracle/reference_port.py) on the host
@@ -298,6 +299,16 @@ def main():
     G = torch.randn(n, M, dtype=torch.float32, device=dev,
                     generator=torch.Generator(device=dev).manual_seed(777 + rank))
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush_rd = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    flush_sink = torch.zeros((), dtype=torch.float32, device=dev)
+
+    def flush_l2():
+        # A write larger than L2 evicts the inputs but leaves ~L2-size of dirty lines whose
+        # write-back would land inside the next timed region (measured: plain TMA reads of G and
+        # K at c1 ran at 4.1 TB/s after a write flush, 4.7 TB/s after write + read); reading a
+        # second buffer larger than L2 evicts those too.
+        flush.zero_()
+        torch.sum(flush_rd, dim=0, out=flush_sink)
     compute = shard.NativeShardCompute()
     route = None
     dy_reduce = "none"
@@ -341,7 +352,7 @@ def main():
     stream = torch.cuda.current_stream(dev)
     evs = []
     for _ in range(args.steps):
-        flush.zero_()
+        flush_l2()
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
@@ -362,7 +373,7 @@ def main():
     def time_alone(gr, reps):
         out = []
         for _ in range(reps):
-            flush.zero_()
+            flush_l2()
             a = torch.cuda.Event(enable_timing=True)
             b = torch.cuda.Event(enable_timing=True)
             a.record(stream)
@@ -420,7 +431,7 @@ def main():
             "config": {"workload": f"{args.config}: RBF fwd+bwd fp32, {n} rows of X per rank "
                                    f"(N={Ng} total), M={M}, D={D}, gamma={g:.6g}",
                        "N": Ng, "M": M, "D": D, "rows_per_rank": n,
-                       "l2": "flushed before every timed step (256 MiB write, outside events)",
+                       "l2": "flushed before every timed step (256 MiB write + 256 MiB read, outside events)",
                        "parallelism": f"row-shard x{world}" + (
                            ", dY reduced in the backward over NVLink peer memory"
                            if dy_reduce == "peer" else ", dY all-reduce (NCCL)"
