@@ -56,6 +56,10 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="target CPU seconds of the cpu_baseline sample")
+    ap.add_argument("--case", choices=("rbf", "cosine_sim"), default="rbf",
+                    help="rbf (the headline) or the cosine-similarity case (one GPU)")
+    ap.add_argument("--cos-size", type=int, default=4096,
+                    help="N = M of the cosine-similarity workload (D = 64)")
     return ap.parse_args()
 
 
@@ -194,6 +198,24 @@ class ClockSampler:
                 "samples": len(sm), "source": "nvidia-smi"}
 
 
+class L2Flush:
+    """Evicts L2 between timed steps.  A write larger than L2 evicts the inputs but leaves
+    ~L2-size of dirty lines whose write-back would land inside the next timed region (measured:
+    plain TMA reads of G and K at c1 ran at 4.1 TB/s after a write flush, 4.7 TB/s after write +
+    read); reading a second buffer larger than L2 evicts those too."""
+
+    def __init__(self, dev):
+        import torch
+        self.torch = torch
+        self.w = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        self.r = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+        self.sink = torch.zeros((), dtype=torch.float32, device=dev)
+
+    def __call__(self):
+        self.w.zero_()
+        self.torch.sum(self.r, dim=0, out=self.sink)
+
+
 def nvsmi_id(device):
     import torch
     try:
@@ -275,6 +297,11 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.case == "cosine_sim":
+        if world > 1:
+            raise SystemExit("--case cosine_sim runs on one GPU")
+        run_cosine(args)
+        return
     if args.impl == "reference":
         run_reference(args, world, rank)
         return
@@ -298,17 +325,7 @@ def main():
     del X_all
     G = torch.randn(n, M, dtype=torch.float32, device=dev,
                     generator=torch.Generator(device=dev).manual_seed(777 + rank))
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    flush_rd = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
-    flush_sink = torch.zeros((), dtype=torch.float32, device=dev)
-
-    def flush_l2():
-        # A write larger than L2 evicts the inputs but leaves ~L2-size of dirty lines whose
-        # write-back would land inside the next timed region (measured: plain TMA reads of G and
-        # K at c1 ran at 4.1 TB/s after a write flush, 4.7 TB/s after write + read); reading a
-        # second buffer larger than L2 evicts those too.
-        flush.zero_()
-        torch.sum(flush_rd, dim=0, out=flush_sink)
+    flush_l2 = L2Flush(dev)
     compute = shard.NativeShardCompute()
     route = None
     dy_reduce = "none"
@@ -456,6 +473,184 @@ def main():
         sys.stdout.flush()
         sys.stderr.flush()
         os._exit(0)
+
+
+COS_METRIC = "cosine_sim fwd+bwd GFLOP/s at N=M={n} D=64 (one GPU)"
+
+
+def run_cosine(args):
+    """The cosine-similarity case on one GPU: one step = forward S = cos(A, B) + backward
+    (dA, dB) from an upstream dS, fp32.  FLOP per step = 6*N*M*D; algorithmic HBM bytes per step
+    = 8*N*M + 16*(N+M)*D (S written, dS read, rows and gradients).  Same timing rules as the RBF
+    bench (CUDA graph, L2 flushed outside the events, NVML clocks)."""
+    import torch
+    from cases.cosine_sim import config as cos_config
+    from cases.cosine_sim import native as cnative
+    from cases.cosine_sim import op as cop
+    from cases.rbf import native
+    from oracle import reference_port
+
+    n = M = args.cos_size
+    D, eps = 64, cos_config.EPS
+    metric = COS_METRIC.format(n=n)
+    workload_name = f"cosine_sim fwd+bwd fp32, N=M={n}, D={D}, eps={eps:g}"
+    if args.impl == "reference":
+        threads = os.cpu_count() or 1
+        sec, done = reference_port.cos_time_sample(n, M, D, eps, 256, threads,
+                                                   min_seconds=max(1.0, args.cpu_seconds / 4))
+        gf = 6.0 * done * M * D / sec / 1e9
+        print(json.dumps({
+            "impl": "reference", "metric": metric, "value": round(gf, 3), "unit": UNIT,
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(sec / done * n * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": workload_name, "N": n, "M": M, "D": D},
+            "cpu_baseline": {"value": round(gf, 3), "unit": UNIT, "cores": threads,
+                             "kind": "port", "sample": f"{done} rows of A x all {M} rows of B"},
+            "e2e": {"value": round(gf, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
+        return
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(4321)
+    A = torch.randn(n, D, device=dev, generator=gen)
+    B = torch.randn(M, D, device=dev, generator=gen)
+    dS = torch.randn(n, M, device=dev, generator=gen)
+    flush_l2 = L2Flush(dev)
+
+    def fwd():
+        return cnative.forward_with_workspace(A, B, eps)
+
+    S, ws = fwd()
+
+    def bwd():
+        return cnative.cos_backward(dS, n, M, D, eps, workspace=ws)
+
+    def step_fb():
+        S_, ws_ = cnative.forward_with_workspace(A, B, eps)
+        cnative.cos_backward(dS, n, M, D, eps, workspace=ws_)
+
+    for _ in range(max(args.warmup, 0)):
+        step_fb()
+    torch.cuda.synchronize()
+
+    def capture(fn):
+        gr = torch.cuda.CUDAGraph()
+        before = native.launch_count()
+        with torch.cuda.graph(gr):
+            fn()
+        return gr, native.launch_count() - before
+
+    step_graph, launches_per_step = capture(step_fb)
+    fwd_graph, _ = capture(fwd)
+    bwd_graph, _ = capture(bwd)
+    for _ in range(max(args.warmup, 0)):
+        step_graph.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+
+    def time_graph(gr, reps):
+        evs = []
+        for _ in range(reps):
+            flush_l2()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            gr.replay()
+            b.record(stream)
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        return statistics.mean(a.elapsed_time(b) for a, b in evs)
+
+    sampler = ClockSampler(nvsmi_id(dev))
+    sampler.start()
+    ms = time_graph(step_graph, args.steps)
+    clocks = sampler.stop()
+    reps = max(args.steps, 5)
+    ms_fwd = time_graph(fwd_graph, reps)
+    ms_bwd = time_graph(bwd_graph, reps)
+
+    pk = peaks()
+    fwd_bytes = 4 * n * M + 4 * (n + M) * D
+    bwd_bytes = 4 * n * M + 12 * (n + M) * D
+    if ms_bwd >= ms_fwd:
+        kname, kms, kbytes = "cosine backward (prepared)", ms_bwd, bwd_bytes
+    else:
+        kname, kms, kbytes = "cosine forward (normalise + kernel)", ms_fwd, fwd_bytes
+    achieved = kbytes / (kms * 1e-3) / 1e9
+    roofline = {"kernel": kname, "bound": "hbm", "achieved": round(achieved, 1),
+                "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                "traffic": traffic_table().get(f"{kname}|cos{n}"), "peak_source": pk["source"],
+                "algorithmic_bytes_per_launch": kbytes, "ms_per_launch": round(kms, 5)}
+    t_roof = max(6.0 * n * M * D / (pk["bf16_tflops"] / 2.0 * 1e12),
+                 cos_config.hbm_bytes(n, M, D) / (pk["hbm_gbs"] * 1e9))
+    gflops = 6.0 * n * M * D / (ms * 1e-3) / 1e9
+
+    # End to end through the autograd op with pinned host buffers (dS copied in on a side stream
+    # during the forward, S copied out on another during the backward).
+    Ah, Bh, dSh = A.cpu().pin_memory(), B.cpu().pin_memory(), dS.cpu().pin_memory()
+    Sh = torch.empty(n, M).pin_memory()
+    dAh, dBh = torch.empty(n, D).pin_memory(), torch.empty(M, D).pin_memory()
+    h2d, d2h = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+
+    def e2e_once():
+        Ad = Ah.to(dev, non_blocking=True).requires_grad_(True)
+        Bd = Bh.to(dev, non_blocking=True).requires_grad_(True)
+        h2d.wait_stream(stream)
+        with torch.cuda.stream(h2d):
+            dSd = dSh.to(dev, non_blocking=True)
+        dSd.record_stream(stream)
+        Sd = cop.candidate({"A": Ad, "B": Bd}, {"eps": eps})
+        d2h.wait_stream(stream)
+        with torch.cuda.stream(d2h):
+            Sh.copy_(Sd.detach(), non_blocking=True)
+        Sd.record_stream(d2h)
+        stream.wait_stream(h2d)
+        Sd.backward(dSd)
+        dAh.copy_(Ad.grad, non_blocking=True)
+        dBh.copy_(Bd.grad, non_blocking=True)
+        stream.wait_stream(d2h)
+
+    for _ in range(2):
+        e2e_once()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(max(3, min(args.steps, 10))):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        e2e_once()
+        b.record(stream)
+        b.synchronize()
+        times.append(a.elapsed_time(b))
+    e2e_ms = statistics.mean(times)
+    e2e = {"value": round(6.0 * n * M * D / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
+           "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": 4 * (n * D + M * D + n * M),
+           "d2h_bytes_per_step": 4 * (n * M + n * D + M * D),
+           "api": "cases.cosine_sim.op.candidate + autograd"}
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        sec, done = reference_port.cos_time_sample(n, M, D, eps, 512, threads,
+                                                   min_seconds=0.75 * args.cpu_seconds)
+        cpu = {"value": round(6.0 * done * M * D / sec / 1e9, 3), "unit": UNIT, "cores": threads,
+               "kind": "port", "sample": f"{done} rows of A (512 per pass) x all {M} rows of B, "
+                                         f"fwd+bwd ({sec:.1f} s on {threads} threads)"}
+    print(json.dumps({
+        "case": "cosine_sim", "metric": metric, "value": round(gflops, 2), "unit": UNIT,
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded A, B, dS ~ N(0,1))",
+        "config": {"workload": workload_name, "N": n, "M": M, "D": D,
+                   "l2": "flushed before every timed step (256 MiB write + 256 MiB read, outside events)"},
+        "ms_fwd": round(ms_fwd, 5), "ms_bwd": round(ms_bwd, 5),
+        "pct_roofline_step": round(100.0 * t_roof / (ms * 1e-3), 2),
+        "roofline_step_us": round(t_roof * 1e6, 2), "roofline": roofline,
+        "gpu_launches": int(launches_per_step * args.steps), "clocks": clocks, "e2e": e2e,
+        "cpu_baseline": cpu}), flush=True)
+    del step_graph, fwd_graph, bwd_graph
 
 
 def run_e2e(X, Y, G, g, world, dev, args, shard, op, route=None):

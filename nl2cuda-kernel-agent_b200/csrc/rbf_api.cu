@@ -8,6 +8,7 @@
 #include <atomic>
 #include <mutex>
 
+#include "../../include/cos_sm100.h"
 #include "rbf_common.cuh"
 #include "rbf_kernels.cuh"
 
@@ -73,11 +74,12 @@ int check_ptr(const void* p, int64_t elems, const char* name) {
 constexpr int64_t kMaxDim = int64_t(1) << 31;  // rows / cols of one call
 constexpr int64_t kMaxD = 4096;
 
-int check_shape(int64_t N, int64_t M, int64_t D, float gamma) {
+int check_shape(int64_t N, int64_t M, int64_t D, float gamma, bool is_eps = false) {
   if (N < 0 || M < 0 || D < 0) return set_detail(RBF_ERR_INVALID_ARGUMENT, "negative size");
   if (N >= kMaxDim || M >= kMaxDim) return set_detail(RBF_ERR_UNSUPPORTED, "N or M >= 2^31");
   if (D > kMaxD) return set_detail(RBF_ERR_UNSUPPORTED, "D > 4096");
-  if (!std::isfinite(gamma)) return set_detail(RBF_ERR_INVALID_ARGUMENT, "gamma is not finite");
+  if (!std::isfinite(gamma))
+    return set_detail(RBF_ERR_INVALID_ARGUMENT, is_eps ? "eps is not finite" : "gamma is not finite");
   return RBF_OK;
 }
 
@@ -158,6 +160,62 @@ int backward_impl(const float* X, const float* Y, const float* G, const float* K
                        "backward launch");
   return cuda_status(launch_backward_simt(X, Y, G, K, dX, dY, N, M, D, gamma, stream),
                      "backward launch");
+}
+
+// ---- cosine similarity (include/cos_sm100.h): the same split workspace, normalised rows ----
+
+int cos_forward_impl(const float* A, const float* B, float* S, int64_t N, int64_t M, int64_t D,
+                     float eps, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  int st = check_shape(N, M, D, eps, true);
+  if (st) return st;
+  if ((st = check_ptr(A, N * D, "A"))) return st;
+  if ((st = check_ptr(B, M * D, "B"))) return st;
+  if ((st = check_ptr(S, N * M, "S"))) return st;
+  const PrepLayout L = prep_layout(N, M, D);
+  if (ws == nullptr || ws_bytes < L.end) return set_detail(RBF_ERR_WORKSPACE, "forward workspace too small");
+  if (!aligned16(ws)) return set_detail(RBF_ERR_MISALIGNED, "workspace is not 16-byte aligned");
+  if ((st = check_device())) return st;
+  if ((st = cuda_status(launch_prep(A, B, N, M, D, ws, stream, &eps), "normalising split launch")))
+    return st;
+  return cuda_status(launch_forward_tc(A, B, S, N, M, D, 0.f, ws, wait_config_from_env(), stream,
+                                       Epi::kDot),
+                     "forward launch");
+}
+
+// A, B: only when !prepared (the normalising split pass runs first).
+int cos_backward_impl(const float* A, const float* B, const float* dS, float* dA, float* dB,
+                      int64_t N, int64_t M, int64_t D, float eps, void* ws, size_t ws_bytes,
+                      cudaStream_t stream, bool prepared) {
+  int st = check_shape(N, M, D, eps, true);
+  if (st) return st;
+  if (!prepared) {
+    if ((st = check_ptr(A, N * D, "A"))) return st;
+    if ((st = check_ptr(B, M * D, "B"))) return st;
+  }
+  if ((st = check_ptr(dS, N * M, "dS"))) return st;
+  if ((st = check_ptr(dA, N * D, "dA"))) return st;
+  if ((st = check_ptr(dB, M * D, "dB"))) return st;
+  const PrepLayout L = prep_layout(N, M, D);
+  const size_t need = L.end + backward_extra_bytes(N, M, D);
+  if (ws == nullptr || ws_bytes < need) return set_detail(RBF_ERR_WORKSPACE, "backward workspace too small");
+  if (!aligned16(ws)) return set_detail(RBF_ERR_MISALIGNED, "workspace is not 16-byte aligned");
+  if ((st = check_device())) return st;
+  if (!prepared) {
+    if ((st = cuda_status(launch_prep(A, B, N, M, D, ws, stream, &eps), "normalising split launch")))
+      return st;
+  }
+  // gA = dS Bh, gB = dS^T Ah on the tensor cores (or CUDA cores when M % 4 != 0) ...
+  if (backward_tc_supported(N, M, D))
+    st = cuda_status(launch_backward_tc(nullptr, nullptr, dS, nullptr, dA, dB, N, M, D, 0.f, ws,
+                                        wait_config_from_env(), stream, nullptr, Epi::kDot),
+                     "backward launch");
+  else
+    st = cuda_status(launch_backward_simt(nullptr, nullptr, dS, nullptr, dA, dB, N, M, D, 0.f,
+                                          stream, Epi::kDot, ws),
+                     "backward launch");
+  if (st) return st;
+  // ... then through the normalisation, row by row.
+  return cuda_status(launch_cos_finalize(dA, dB, N, M, D, eps, ws, stream), "finalize launch");
 }
 
 }  // namespace
@@ -290,6 +348,34 @@ int rbf_sm100_dy_exchange(float* dY, int64_t M, int64_t D, float* const* dy_buff
   if (const char* s = std::getenv("RBF_XCHG_ONE_PHASE_MAX")) a.one_phase_max = std::atoi(s);
   return cuda_status(launch_dy_exchange(a, reinterpret_cast<cudaStream_t>(stream)),
                      "exchange launch");
+}
+
+size_t cos_sm100_forward_workspace_bytes(int64_t N, int64_t M, int64_t D) {
+  return rbf_sm100_forward_workspace_bytes(N, M, D);
+}
+
+size_t cos_sm100_backward_workspace_bytes(int64_t N, int64_t M, int64_t D) {
+  return rbf_sm100_backward_workspace_bytes(N, M, D);
+}
+
+int cos_sm100_forward(const float* A, const float* B, float* S, int64_t N, int64_t M, int64_t D,
+                      float eps, void* workspace, size_t workspace_bytes, rbf_stream_t stream) {
+  return cos_forward_impl(A, B, S, N, M, D, eps, workspace, workspace_bytes,
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+int cos_sm100_backward_prepared(const float* dS, float* dA, float* dB, int64_t N, int64_t M,
+                                int64_t D, float eps, void* workspace, size_t workspace_bytes,
+                                rbf_stream_t stream) {
+  return cos_backward_impl(nullptr, nullptr, dS, dA, dB, N, M, D, eps, workspace,
+                           workspace_bytes, reinterpret_cast<cudaStream_t>(stream), true);
+}
+
+int cos_sm100_backward(const float* A, const float* B, const float* dS, float* dA, float* dB,
+                       int64_t N, int64_t M, int64_t D, float eps, void* workspace,
+                       size_t workspace_bytes, rbf_stream_t stream) {
+  return cos_backward_impl(A, B, dS, dA, dB, N, M, D, eps, workspace, workspace_bytes,
+                           reinterpret_cast<cudaStream_t>(stream), false);
 }
 
 int rbf_sm100_read_status(void* workspace, rbf_stream_t stream, int* device_status) {

@@ -33,6 +33,10 @@
 // varies between runs.  Features are processed in slices of DS (32 or 64); D > 64 runs one
 // slice per segment (G and K are re-read per slice).  D % 4 != 0 flushes dX with red.add too.
 //
+// The DOT instantiation (cosine similarity, on the normalised rows of the split pass) streams
+// only G (W = G, half the strip bytes), keeps no row / column sums and uses c = -1, so that
+// dX = G Y and dY = G^T X; the per-row normalisation terms are added by cos_finalize_kernel.
+//
 // TMEM (512 columns): [0,64) dY acc | [64,128) dX acc | [128,256) two W buffers (hi 32 + lo
 // 32) | [256,384) W^T hi (128 columns of i) | [384,512) W^T lo.
 // Shared memory (DS = 64): strip ring 4 x 32 KiB, X ring 2 x 16 KiB, Y ring 2 x 16 KiB, dX
@@ -191,12 +195,26 @@ __device__ __forceinline__ void red_add1(float* p, float a) {
 }
 
 // out[r, d0 + e] += c * (s * src[r, d0 + e] - acc[e]) for e < DS, d0 + e < D.
-template <int DS>
+// out[r, d0..] += c * (s * src[r, d0..] - acc); SUM = false: out += -c * acc (src not read).
+template <int DS, bool SUM = true>
 __device__ __forceinline__ void flush_row(float* out, const float* src, int64_t r, int64_t D,
                                           int d0, float c, float s, const uint32_t* acc) {
   float* o = out + r * D + d0;
   const float* x = src + r * D + d0;
   const int n = (D - d0) < DS ? (int)(D - d0) : DS;
+  if (!SUM) {
+    if (n == DS && (D & 3) == 0) {
+#pragma unroll
+      for (int e = 0; e < DS; e += 4)
+        red_add4(o + e, -c * __uint_as_float(acc[e]), -c * __uint_as_float(acc[e + 1]),
+                 -c * __uint_as_float(acc[e + 2]), -c * __uint_as_float(acc[e + 3]));
+    } else {
+#pragma unroll
+      for (int e = 0; e < DS; ++e)
+        if (e < n) red_add1(o + e, -c * __uint_as_float(acc[e]));
+    }
+    return;
+  }
   if (n == DS && (D & 3) == 0) {
 #pragma unroll
     for (int e = 0; e < DS; e += 4) {
@@ -238,7 +256,7 @@ __device__ __forceinline__ void tmem_st_n(uint32_t taddr, const uint32_t* r) {
 #endif
 constexpr int CB = RBF_CB;  // rows of W^T a C-warp converts per TMEM store (code size vs. batching)
 
-template <int DS>
+template <int DS, bool DOT = false>
 __global__ void __launch_bounds__(THREADS, 1)
     rbf_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_g,
                       const __grid_constant__ CUtensorMap tm_k,
@@ -307,7 +325,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   if (warp == 0 && lane == 0) {
     ptx::prefetch_tensormap(&tm_g);
-    ptx::prefetch_tensormap(&tm_k);
+    if (!DOT) ptx::prefetch_tensormap(&tm_k);
     ptx::prefetch_tensormap(&tm_yhi);
     ptx::prefetch_tensormap(&tm_ylo);
     if (a.tma_flush) ptx::prefetch_tensormap(&tm_dx);
@@ -386,9 +404,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             skipped = true;  // test hook: this strip never arrives, its consumers time out
           } else {
             uint8_t* sm = ring + s * 2 * STRIP;
-            ptx::mbar_arrive_expect_tx(&full[s], 2 * STRIP);
+            ptx::mbar_arrive_expect_tx(&full[s], DOT ? STRIP : 2 * STRIP);
             ptx::tma_load_2d_hint(sm, &tm_g, j0 + SR * s, i0, &full[s], stream);
-            ptx::tma_load_2d_hint(sm + STRIP, &tm_k, j0 + SR * s, i0, &full[s], stream);
+            if (!DOT) ptx::tma_load_2d_hint(sm + STRIP, &tm_k, j0 + SR * s, i0, &full[s], stream);
             issued |= 1u << s;
             last = (last & ~(1u << s)) | (ph << s);
           }
@@ -619,9 +637,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int r = 0; r < CB; ++r) {
             const uint32_t off = (uint32_t)(r0 + r) * 128 + coff[r & 7];
-            const float w = *reinterpret_cast<const float*>(gb + off) *
-                            *reinterpret_cast<const float*>(kb + off);
-            colsum += w;
+            float w = *reinterpret_cast<const float*>(gb + off);
+            if (!DOT) {
+              w *= *reinterpret_cast<const float*>(kb + off);
+              colsum += w;
+            }
             float hh, ll;
             tf32_split(w, hh, ll);
             hi[r] = __float_as_uint(hh);
@@ -653,7 +673,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (a.ablate & 32) continue;
 #endif
         float* dst = a.route.world > 0 ? route_dst : a.dY;
-        if (j < a.M) flush_row<DS>(dst, a.Y, j, a.D, tc.slice * DS, a.c, colsum, accv);
+        if (j < a.M) flush_row<DS, !DOT>(dst, a.Y, j, a.D, tc.slice * DS, a.c, colsum, accv);
         if (lane == 0 && q == 0) TRACE(4, 50);
       }
     }
@@ -680,12 +700,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(dx_empty);
       if (!a.tma_flush) {
-        if (prev_i < a.N) flush_row<DS>(a.dX, a.X, prev_i, a.D, prev_d0, a.c, prev_rowsum, accv);
+        if (prev_i < a.N) flush_row<DS, !DOT>(a.dX, a.X, prev_i, a.D, prev_d0, a.c, prev_rowsum, accv);
         return true;
       }
       // -c * acc goes through shared memory to a TMA reduce-add (32 rows x DS, coalesced in L2);
       // c * rowsum * x is added once per row by the finalize pass from the rowsum vector.
-      if (prev_i < a.N && prev_d0 == 0 && !(a.ablate & 2)) red_add1(a.rowsum + prev_i, prev_rowsum);
+      if (!DOT && prev_i < a.N && prev_d0 == 0 && !(a.ablate & 2))
+        red_add1(a.rowsum + prev_i, prev_rowsum);
       uint8_t* stg = staging + q * C::STAGING;
       if (lane == 0) ptx::bulk_wait_read<0>();  // the previous reduce has read the buffer
       __syncwarp();
@@ -731,11 +752,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 #endif
           const int off = (c4 ^ (lane & 7)) << 4;
           const float4 g = *reinterpret_cast<const float4*>(gb + off);
-          const float4 k = *reinterpret_cast<const float4*>(kb + off);
-          const float w[4] = {g.x * k.x, g.y * k.y, g.z * k.z, g.w * k.w};
+          float w[4] = {g.x, g.y, g.z, g.w};
+          if (!DOT) {
+            const float4 k = *reinterpret_cast<const float4*>(kb + off);
+            w[0] *= k.x; w[1] *= k.y; w[2] *= k.z; w[3] *= k.w;
+          }
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            rowsum += w[e];
+            if (!DOT) rowsum += w[e];
             float h, l;
             tf32_split(w[e], h, l);
             hi[4 * c4 + e] = __float_as_uint(h);
@@ -852,8 +876,9 @@ bool backward_tc_supported(int64_t N, int64_t M, int64_t D) {
 cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, const float* K,
                                float* dX, float* dY, int64_t N, int64_t M, int64_t D,
                                float gamma, void* ws, const WaitConfig& wc, cudaStream_t stream,
-                               const DyRoute* route) {
+                               const DyRoute* route, Epi epi) {
   cudaError_t e;
+  const bool dot = epi == Epi::kDot;
   const bool routed = route != nullptr && route->world > 0;
   const PrepLayout L = prep_layout(N, M, D);
   const bool tma_flush = (D % 4) == 0;  // dX rows 16-byte pitched
@@ -885,7 +910,8 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
   const int DS = (D <= 32) ? 32 : 64;
   const int mn = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
   CUtensorMap tg, tk, txh, txl, tyh, tyl, tdx;
-  if (!make_tmap_2d(&tg, G, N, M, M, 32, 128) || !make_tmap_2d(&tk, K, N, M, M, 32, 128) ||
+  if (!make_tmap_2d(&tg, G, N, M, M, 32, 128) ||
+      !make_tmap_2d(&tk, dot ? G : K, N, M, M, 32, 128) ||  // DOT: not read
       !make_tmap_2d(&txh, ws_at<float>(ws, L.xhi), N, L.Dp, L.Dp, 32, 32, mn) ||
       !make_tmap_2d(&txl, ws_at<float>(ws, L.xlo), N, L.Dp, L.Dp, 32, 32, mn) ||
       !make_tmap_2d(&tyh, ws_at<float>(ws, L.yhi), M, L.Dp, L.Dp, 32, 32, mn) ||
@@ -925,7 +951,7 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
     const int64_t rows = a.total_tiles / group;
     a.static_rows = rows - rows * pct / 100;
   }
-  a.c = -2.f * gamma;
+  a.c = dot ? -1.f : -2.f * gamma;
   a.status = ws_at<int>(ws, L.status);
   a.timeout_ns = wc.timeout_ns;
   a.debug_skip_first_load = wc.debug_skip_first_load;
@@ -933,23 +959,23 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
 #ifdef RBF_TRACE
   if (const char* ab = std::getenv("RBF_ABLATE")) a.ablate = std::atoi(ab);
 #endif
-  if (DS == 32) {
-    if ((e = cudaFuncSetAttribute(rbf_bwd_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)Cfg<32>::SMEM)) != cudaSuccess)
-      return e;
-    e = launch_kernel(rbf_bwd_tc_kernel<32>, dim3(grid), dim3(THREADS), Cfg<32>::SMEM, stream, tg,
-                      tk, txh, txl, tyh, tyl, tdx, a);
-  } else {
-    if ((e = cudaFuncSetAttribute(rbf_bwd_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)Cfg<64>::SMEM)) != cudaSuccess)
-      return e;
-    e = launch_kernel(rbf_bwd_tc_kernel<64>, dim3(grid), dim3(THREADS), Cfg<64>::SMEM, stream, tg,
-                      tk, txh, txl, tyh, tyl, tdx, a);
-  }
+  auto launch = [&](auto kernel, size_t smem) -> cudaError_t {
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem);
+    if (err != cudaSuccess) return err;
+    return launch_kernel(kernel, dim3(grid), dim3(THREADS), smem, stream, tg, tk, txh, txl, tyh,
+                         tyl, tdx, a);
+  };
+  if (DS == 32)
+    e = dot ? launch(rbf_bwd_tc_kernel<32, true>, Cfg<32>::SMEM)
+            : launch(rbf_bwd_tc_kernel<32, false>, Cfg<32>::SMEM);
+  else
+    e = dot ? launch(rbf_bwd_tc_kernel<64, true>, Cfg<64>::SMEM)
+            : launch(rbf_bwd_tc_kernel<64, false>, Cfg<64>::SMEM);
   if (e != cudaSuccess) return e;
   note_launches(1);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  if (tma_flush) {
+  if (tma_flush && !dot) {
     const int64_t n4 = N * (D / 4);
     if ((e = launch_kernel(rbf_bwd_finalize_kernel, dim3((unsigned)ceil_div(n4, 256)), dim3(256), 0,
                            stream, X, rowsum, dX, N, D, a.c)) != cudaSuccess)

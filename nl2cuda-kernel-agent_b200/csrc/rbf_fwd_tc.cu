@@ -25,6 +25,9 @@
 // returns.
 //
 // HBM roofline per launch: K write 4*N*M bytes + X/Y split reads; tensor work 3 * 2*N*M*Dp.
+//
+// The DOT instantiation stores x_i.y_j itself (no norms, no exp): with rows the split pass
+// normalised, that is the cosine-similarity matrix S[i,j] = a_i.b_j / (|a_i| |b_j|).
 #include <cuda.h>
 
 #include <algorithm>
@@ -110,7 +113,7 @@ __device__ __forceinline__ void ftrace(int role, int code) {
 #define FTRACE(role, code) ((void)0)
 #endif
 
-template <bool TMA_STORE, bool RES_A, bool PAIR>
+template <bool TMA_STORE, bool RES_A, bool PAIR, bool DOT = false>
 __global__ void __launch_bounds__(THREADS, 1)
     rbf_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_xhi,
                       const __grid_constant__ CUtensorMap tm_xlo,
@@ -414,13 +417,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     // The norms of the next tile are loaded one whole tile ahead (the first touch of a column
     // block after an L2 flush misses to DRAM): each lane holds ||y||^2 of its own column in the
     // two 32-column chunks and the chunk's 32 values are broadcast with warp shuffles.
+    // (The dot-product epilogue uses no norms.)
     auto load_yn = [&](int64_t t, int c) {
       const int64_t j = (t % a.tiles_n) * BN + h * (32 * CPW) + c * 32 + lane;
-      return j < a.M ? __ldg(a.yn + j) : 0.f;
+      return !DOT && j < a.M ? __ldg(a.yn + j) : 0.f;
     };
     auto load_xn = [&](int64_t t) {
       const int64_t i = (t / a.tiles_n) * TILE_ROWS + rank * BM + q * 32 + lane;
-      return i < a.N ? __ldg(a.xn + i) : 0.f;
+      return !DOT && i < a.N ? __ldg(a.xn + i) : 0.f;
     };
     float xnext = 0.f, ynext[CPW];
 #pragma unroll
@@ -472,9 +476,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         float out[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          const float yj = __shfl_sync(0xffffffffu, ylane[c], e);
-          const float d2 = fmaxf(fmaf(-2.f, __uint_as_float(v[e]), xi + yj), 0.f);
-          out[e] = exp2_approx(d2 * a.scale);
+          if (DOT) {
+            out[e] = __uint_as_float(v[e]);
+          } else {
+            const float yj = __shfl_sync(0xffffffffu, ylane[c], e);
+            const float d2 = fmaxf(fmaf(-2.f, __uint_as_float(v[e]), xi + yj), 0.f);
+            out[e] = exp2_approx(d2 * a.scale);
+          }
         }
 #ifdef RBF_TRACE
         if (lane == 0 && warp == 2) FTRACE(2, 70 + c);
@@ -625,7 +633,7 @@ static cudaError_t pair_capacity(int* clusters) {
 
 cudaError_t launch_forward_tc(const float* X, const float* Y, float* K, int64_t N, int64_t M,
                               int64_t D, float gamma, void* ws, const WaitConfig& wc,
-                              cudaStream_t stream) {
+                              cudaStream_t stream, Epi epi) {
   (void)X; (void)Y;
   if (N == 0 || M == 0) return cudaSuccess;
   const PrepLayout L = prep_layout(N, M, D);
@@ -662,7 +670,7 @@ cudaError_t launch_forward_tc(const float* X, const float* Y, float* K, int64_t 
   const bool res_a = a.num_kc <= RA_CHUNKS;
   // Pair variant: D <= 64, TMA-stored K, and enough two-CTA clusters resident at once.
   int pair_clusters = 0;
-  if (res_a && tma_store && wc.fwd_pair) {
+  if (res_a && tma_store && wc.fwd_pair && epi == Epi::kRbf) {
     if ((e = pair_capacity(&pair_clusters)) != cudaSuccess) return e;
   }
   if (pair_clusters > 0) {
@@ -689,12 +697,20 @@ cudaError_t launch_forward_tc(const float* X, const float* Y, float* K, int64_t 
       return launch_kernel(kernel, dim3(grid), dim3(THREADS), smem, stream, txh, txl, tyh, tyl,
                            tk, a);
     };
-    if (tma_store)
+    if (epi == Epi::kDot) {
+      if (tma_store)
+        e = res_a ? launch(rbf_fwd_tc_kernel<true, true, false, true>, SMEM_BYTES_RA)
+                  : launch(rbf_fwd_tc_kernel<true, false, false, true>, SMEM_BYTES);
+      else
+        e = res_a ? launch(rbf_fwd_tc_kernel<false, true, false, true>, SMEM_BYTES_RA)
+                  : launch(rbf_fwd_tc_kernel<false, false, false, true>, SMEM_BYTES);
+    } else if (tma_store) {
       e = res_a ? launch(rbf_fwd_tc_kernel<true, true, false>, SMEM_BYTES_RA)
                 : launch(rbf_fwd_tc_kernel<true, false, false>, SMEM_BYTES);
-    else
+    } else {
       e = res_a ? launch(rbf_fwd_tc_kernel<false, true, false>, SMEM_BYTES_RA)
                 : launch(rbf_fwd_tc_kernel<false, false, false>, SMEM_BYTES);
+    }
   }
   if (e != cudaSuccess) return e;
   note_launches(1);

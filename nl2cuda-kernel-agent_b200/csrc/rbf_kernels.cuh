@@ -75,14 +75,23 @@ struct DyRoute {
   int world, rank;
 };
 
+// What the tensor-core kernels compute from the X.Y^T contraction:
+//   kRbf: the forward stores exp(-gamma * (|x|^2 + |y|^2 - 2 x.y)); the backward's W = G o K
+//         and it adds the row / column sum terms (the Gaussian RBF case);
+//   kDot: the forward stores x.y; the backward's W = G (no K) and it adds nothing else, so
+//         dX = G Y and dY = G^T X (the cosine-similarity case, on rows the split pass
+//         normalised; cos_finalize_kernel turns these into the gradients of the raw rows).
+enum class Epi { kRbf, kDot };
+
 // rbf_fwd_tc.cu: the tcgen05 3xTF32 forward (workspace must hold the split pass output).
 cudaError_t launch_forward_tc(const float* X, const float* Y, float* K, int64_t N, int64_t M,
                               int64_t D, float gamma, void* ws, const WaitConfig& wc,
-                              cudaStream_t stream);
+                              cudaStream_t stream, Epi epi = Epi::kRbf);
 
-// rbf_prep.cu: norms + TF32 hi/lo split of X and Y into the workspace.
+// rbf_prep.cu: norms + TF32 hi/lo split of X and Y into the workspace.  normalize_eps != NULL:
+// the rows are first divided by (||row|| + *normalize_eps) and the norms (not squared) stored.
 cudaError_t launch_prep(const float* X, const float* Y, int64_t N, int64_t M, int64_t D,
-                        void* ws, cudaStream_t stream);
+                        void* ws, cudaStream_t stream, const float* normalize_eps = nullptr);
 
 // rbf_fwd_tc.cu host helpers shared by the tensor-core kernels.
 bool make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
@@ -95,10 +104,11 @@ int device_sm_count();
 bool backward_tc_supported(int64_t N, int64_t M, int64_t D);
 // Workspace bytes the tensor-core backward needs after the split-pass layout (rowsum vector).
 size_t backward_scratch_bytes(int64_t N, int64_t M, int64_t D);
+// Epi::kDot: K is not read (may be NULL) and gamma is ignored.
 cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, const float* K,
                                float* dX, float* dY, int64_t N, int64_t M, int64_t D,
                                float gamma, void* ws, const WaitConfig& wc, cudaStream_t stream,
-                               const DyRoute* route = nullptr);
+                               const DyRoute* route = nullptr, Epi epi = Epi::kRbf);
 
 // rbf_exchange.cu: completes a routed step -- barrier, owners reduce their j-blocks over every
 // rank's slot, barrier, every rank gathers dY from the owners, the step counter advances.
@@ -116,9 +126,17 @@ struct ExchangeArgs {
 };
 cudaError_t launch_dy_exchange(const ExchangeArgs& a, cudaStream_t stream);
 
-// rbf_simt.cu: fp32 CUDA-core backward for M % 4 != 0.
+// rbf_simt.cu: fp32 CUDA-core backward for M % 4 != 0.  Epi::kDot: W = G, K unused, and the
+// rows multiplied are the normalised ones of the split workspace `ws`.
 cudaError_t launch_backward_simt(const float* X, const float* Y, const float* G, const float* K,
                                  float* dX, float* dY, int64_t N, int64_t M, int64_t D,
-                                 float gamma, cudaStream_t stream);
+                                 float gamma, cudaStream_t stream, Epi epi = Epi::kRbf,
+                                 const void* ws = nullptr);
+
+// cos_finalize.cu: turns gA = dS Bh and gB = dS^T Ah (in dA, dB, in place) into the gradients of
+// the raw rows, dA = gA / (|a| + eps) - (Ah . gA) Ah / |a|  (the second term 0 for a zero row),
+// reading Ah = hi + lo and |a| from a workspace the normalising split pass filled.
+cudaError_t launch_cos_finalize(float* dA, float* dB, int64_t N, int64_t M, int64_t D, float eps,
+                                const void* ws, cudaStream_t stream);
 
 }  // namespace rbf

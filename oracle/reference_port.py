@@ -56,3 +56,38 @@ def time_sample(N, M, D, gamma, sample_rows, threads, seed=0, block_rows=256, mi
         el = time.perf_counter() - t0
         if el >= min_seconds:
             return el, done
+
+
+# ---- cosine similarity: the reference's cases/cosine_sim/reference.py:14-21 + autograd ------
+
+def cos_forward_backward_block(Ab, B, dSb, eps):
+    """Reference forward + autograd backward on one block of A rows -> (S, dA, dB_partial)."""
+    Ab = Ab.detach().clone().requires_grad_(True)
+    Bl = B.detach().clone().requires_grad_(True)
+    Ah = Ab / (Ab.norm(dim=-1, keepdim=True) + eps)
+    Bh = Bl / (Bl.norm(dim=-1, keepdim=True) + eps)
+    S = (Ah.unsqueeze(1) * Bh.unsqueeze(0)).sum(dim=-1)
+    S.backward(dSb)
+    return S.detach(), Ab.grad, Bl.grad
+
+
+def cos_time_sample(N, M, D, eps, sample_rows, threads, seed=0, block_rows=256, min_seconds=0.0):
+    """Seconds for the reference cosine forward + backward of ``sample_rows`` rows of A against
+    all M rows of B, using ``threads`` intra-op threads.  Returns (seconds, rows_done)."""
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(seed)
+    rows = max(1, min(sample_rows, N))
+    A = torch.randn(rows, D, generator=g)
+    B = torch.randn(M, D, generator=g)
+    dS = torch.randn(rows, M, generator=g)
+    cos_forward_backward_block(A[:min(rows, 8)], B, dS[:min(rows, 8)], eps)  # warm-up
+    t0 = time.perf_counter()
+    done = 0
+    while True:
+        for a in range(0, rows, block_rows):
+            b = min(rows, a + block_rows)
+            cos_forward_backward_block(A[a:b], B, dS[a:b], eps)
+        done += rows
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            return el, done

@@ -1,6 +1,7 @@
-"""The C-ABI library loads, exports every symbol include/rbf_sm100.h declares, and rejects bad
-arguments on the host (no GPU needed; no compute call is made)."""
+"""The C-ABI library loads, exports every symbol include/*.h declares (rbf_sm100.h and
+cos_sm100.h), and rejects bad arguments on the host (no GPU needed; no compute call is made)."""
 import ctypes
+import glob
 import os
 import re
 
@@ -9,14 +10,14 @@ import pytest
 from conftest import has_gpu
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADER = os.path.join(ROOT, "include", "rbf_sm100.h")
+HEADERS = sorted(glob.glob(os.path.join(ROOT, "include", "*.h")))
 
 RBF_OK, INVALID, MISALIGNED, WORKSPACE, UNSUPPORTED, CUDA, NO_DEVICE = 0, 1, 2, 3, 4, 5, 6
 
 
 def declared_functions():
-    text = open(HEADER).read()
-    return sorted(set(re.findall(r"RBF_API\s+[\w\s\*]+?\b(rbf_\w+)\s*\(", text)))
+    text = "".join(open(h).read() for h in HEADERS)
+    return sorted(set(re.findall(r"RBF_API\s+[\w\s\*]+?\b((?:rbf|cos)_\w+)\s*\(", text)))
 
 
 @pytest.fixture(scope="module")
@@ -29,7 +30,9 @@ def test_header_declares_the_boundary():
     fns = declared_functions()
     for f in ("rbf_sm100_forward", "rbf_sm100_backward", "rbf_sm100_forward_workspace_bytes",
               "rbf_sm100_backward_workspace_bytes", "rbf_sm100_strerror", "rbf_forward_cuda",
-              "rbf_backward_cuda"):
+              "rbf_backward_cuda", "cos_sm100_forward", "cos_sm100_backward",
+              "cos_sm100_backward_prepared", "cos_sm100_forward_workspace_bytes",
+              "cos_sm100_backward_workspace_bytes"):
         assert f in fns
 
 
@@ -87,3 +90,29 @@ def test_native_refuses_cpu_tensors():
         native.rbf_forward(X, X, 0.5)
     with pytest.raises(RuntimeError, match="CUDA"):
         op.candidate({"X": X, "Y": X}, {"gamma": 0.5})
+
+
+def test_cosine_host_side_validation(lib):
+    from cases.cosine_sim import native as cos_native
+    L = cos_native.lib()
+    vp = ctypes.c_void_p
+    A = 1 << 20
+    wsb = L.cos_sm100_backward_workspace_bytes(8, 8, 4)
+    assert wsb >= L.cos_sm100_forward_workspace_bytes(8, 8, 4) > 0
+
+    def fwd(a, b, s, N, M, D, eps, ws, n):
+        return L.cos_sm100_forward(vp(a), vp(b), vp(s), N, M, D, ctypes.c_float(eps), vp(ws), n,
+                                   vp(0))
+
+    def bwd(ds, da, db, N, M, D, eps, ws, n):
+        return L.cos_sm100_backward_prepared(vp(ds), vp(da), vp(db), N, M, D,
+                                             ctypes.c_float(eps), vp(ws), n, vp(0))
+
+    assert fwd(A, A, A, 8, -1, 4, 1e-8, A, wsb) == INVALID
+    assert fwd(A, A, A, 8, 8, 4, float("inf"), A, wsb) == INVALID
+    assert b"eps" in lib.rbf_sm100_last_error_detail()
+    assert fwd(A, A + 8, A, 8, 8, 4, 1e-8, A, wsb) == MISALIGNED
+    assert fwd(A, A, A, 8, 8, 4, 1e-8, A, 16) == WORKSPACE
+    assert bwd(A, A, A, 8, 8, 4, 1e-8, A, wsb - 1) == WORKSPACE
+    assert bwd(0, A, A, 8, 8, 4, 1e-8, A, wsb) == INVALID
+    assert bwd(A, A, A, 8, 8, 5000, 1e-8, A, 1 << 30) == UNSUPPORTED
