@@ -391,47 +391,85 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         return true;
       };
-      int64_t t = fetch();
-      for (; t >= 0 && ok; ph ^= 1) {
-        const TileCoord tc = tile_of(t, a);
-        const int64_t nxt = fetch();
-        if (!publish(t, nxt < 0 || !same_segment(tile_of(nxt, a), tc))) { ok = false; break; }
-        const int i0 = tc.ib * BT, j0 = tc.jb * BT, d0 = tc.slice * DS;
-        for (int s = 0; s < 4; ++s) {
-          if (!ptx::mbar_wait_bounded(&empty[s], ph ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
-          TRACE(0, 10 + s);
+      // Two cursors, each issued as soon as its own ring has room: the G/K strips (stage s of
+      // every tile, freed by the R-warps and C-warp s) and the Y rows of each strip (2-deep
+      // ring, freed by the dX MMAs).  Issuing them in one blocking sequence would hold strip
+      // s+2 of a tile behind the dX MMAs of strip s.  Tile k's coordinates sit in slot k & 1;
+      // the Y cursor lags the strip cursor by at most one tile.
+      TileCoord slot0 = {0, 0, 0}, slot1 = {0, 0, 0};
+      uint32_t n_strips = 0, n_ys = 0;  // strips / Y loads issued so far
+      int ss = 4;                       // next strip of the current tile (4 = start a new tile)
+      int64_t t = fetch(), nxt = -1;
+      bool strips_done = t < 0;
+      int i0 = 0, j0 = 0;
+      uint64_t idle_since = ptx::globaltimer();
+      while (ok) {
+        bool progressed = false;
+        if (!strips_done && ss == 4 && n_ys + 4 >= n_strips) {
+          const TileCoord tc = tile_of(t, a);
+          nxt = fetch();
+          if (!publish(t, nxt < 0 || !same_segment(tile_of(nxt, a), tc))) { ok = false; break; }
+          if ((n_strips >> 2) & 1u) slot1 = tc; else slot0 = tc;
+          i0 = tc.ib * BT;
+          j0 = tc.jb * BT;
+          ss = 0;
+        }
+        if (!strips_done && ss < 4 && ptx::mbar_test_wait(&empty[ss], ph ^ 1)) {
+          TRACE(0, 10 + ss);
           if (a.debug_skip_first_load && !skipped && blockIdx.x == 0) {
             skipped = true;  // test hook: this strip never arrives, its consumers time out
           } else {
-            uint8_t* sm = ring + s * 2 * STRIP;
-            ptx::mbar_arrive_expect_tx(&full[s], DOT ? STRIP : 2 * STRIP);
-            ptx::tma_load_2d_hint(sm, &tm_g, j0 + SR * s, i0, &full[s], stream);
-            if (!DOT) ptx::tma_load_2d_hint(sm + STRIP, &tm_k, j0 + SR * s, i0, &full[s], stream);
-            issued |= 1u << s;
-            last = (last & ~(1u << s)) | (ph << s);
+            uint8_t* sm = ring + ss * 2 * STRIP;
+            ptx::mbar_arrive_expect_tx(&full[ss], DOT ? STRIP : 2 * STRIP);
+            ptx::tma_load_2d_hint(sm, &tm_g, j0 + SR * ss, i0, &full[ss], stream);
+            if (!DOT) ptx::tma_load_2d_hint(sm + STRIP, &tm_k, j0 + SR * ss, i0, &full[ss], stream);
+            issued |= 1u << ss;
+            last = (last & ~(1u << ss)) | (ph << ss);
           }
-          // Y rows of the strip's 32 columns (B operand of the dX product).
-          if (!ptx::mbar_wait_bounded(&yempty[yst], yph ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
+          ++n_strips;
+          if (++ss == 4) {
+            ph ^= 1;
+            t = nxt;
+            strips_done = t < 0;
+          }
+          progressed = true;
+        }
+        if (n_ys < n_strips && ptx::mbar_test_wait(&yempty[yst], yph ^ 1)) {
+          const TileCoord ty = ((n_ys >> 2) & 1u) ? slot1 : slot0;
+          const int sy = (int)(n_ys & 3u);
           uint8_t* ym = yring + yst * 2 * C::X_BYTES;
 #ifdef RBF_TRACE
           if (a.ablate & 64) {
             ptx::mbar_arrive(&yfull[yst]);
-            if (++yst == YSTAGES) { yst = 0; yph ^= 1; }
-            continue;
-          }
+          } else
 #endif
-          ptx::mbar_arrive_expect_tx(&yfull[yst], 2 * C::X_BYTES);
+          {
+            ptx::mbar_arrive_expect_tx(&yfull[yst], 2 * C::X_BYTES);
 #pragma unroll
-          for (int b = 0; b < DS / 32; ++b) {
-            ptx::tma_load_2d_hint(ym + b * BOX, &tm_yhi, d0 + 32 * b, j0 + SR * s, &yfull[yst], keep);
-            ptx::tma_load_2d_hint(ym + C::X_BYTES + b * BOX, &tm_ylo, d0 + 32 * b, j0 + SR * s,
-                                  &yfull[yst], keep);
+            for (int b = 0; b < DS / 32; ++b) {
+              ptx::tma_load_2d_hint(ym + b * BOX, &tm_yhi, ty.slice * DS + 32 * b,
+                                    ty.jb * BT + SR * sy, &yfull[yst], keep);
+              ptx::tma_load_2d_hint(ym + C::X_BYTES + b * BOX, &tm_ylo, ty.slice * DS + 32 * b,
+                                    ty.jb * BT + SR * sy, &yfull[yst], keep);
+            }
+            yissued |= 1u << yst;
+            ylast = (ylast & ~(1u << yst)) | (yph << yst);
           }
-          yissued |= 1u << yst;
-          ylast = (ylast & ~(1u << yst)) | (yph << yst);
           if (++yst == YSTAGES) { yst = 0; yph ^= 1; }
+          ++n_ys;
+          progressed = true;
         }
-        t = nxt;
+        if (strips_done && n_ys == n_strips) break;
+        if (progressed) {
+          idle_since = ptx::globaltimer();
+        } else {
+          if (ptx::globaltimer() - idle_since > a.timeout_ns) {
+            atomicExch(a.status, RBF_ERR_TIMEOUT);
+            ok = false;
+            break;
+          }
+          __nanosleep(32);  // neither ring has room: leave the issue slots to the other warps
+        }
       }
       if (ok && !publish(-1, true)) ok = false;
       if (!ok) {  // let every copy this thread issued land before the CTA exits

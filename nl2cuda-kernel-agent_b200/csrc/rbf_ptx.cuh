@@ -53,6 +53,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe: has phase `parity` of `bar` completed?  (test_wait never suspends the
+// thread, so one thread can poll several barriers.)
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Slow path of mbar_wait_bounded, kept out of line so that the many wait sites of the
 // persistent kernels share one copy of the polling loop (instruction-cache footprint).
 #ifdef RBF_WAIT_INLINE
