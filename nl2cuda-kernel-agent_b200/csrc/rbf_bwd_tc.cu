@@ -695,6 +695,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0 && q == 0) TRACE(4, 30 + h);
       }
       if (!ok) break;
+      // The stage is refilled by TMA (async proxy) after this release; the warp's reads of it
+      // (generic proxy) must be ordered before that write by a proxy fence, or the refill can
+      // overwrite data a lane has not read yet (measured: wrong dX tiles, a few in 100 runs).
+      ptx::fence_proxy_async_smem();
+      __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&empty[q]);
       if (lane == 0 && (q == 0 || q == 3)) TRACE(q == 0 ? 4 : 6, 40);
       if (seg_end) {
@@ -804,6 +809,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             lo[4 * c4 + e] = __float_as_uint(l);
           }
         }
+        ptx::fence_proxy_async_smem();  // generic reads before the TMA refill (see C-warps)
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&empty[s]);
         if (!ptx::mbar_wait_bounded(&w_empty[wb], bit_of(we_ph, wb) ^ 1, a.status, a.timeout_ns)) { ok = false; break; }

@@ -165,7 +165,9 @@ __device__ __forceinline__ void bulk_wait() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Make generic-proxy writes to shared memory visible to the async proxy (TMA store, MMA).
+// Order this thread's generic-proxy accesses of shared memory before later async-proxy ones
+// (TMA, MMA): writes become visible to a TMA store / MMA read, and reads complete before a TMA
+// load that reuses the buffer after an mbarrier release.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

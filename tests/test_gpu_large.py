@@ -79,3 +79,28 @@ def test_backward_is_linear_in_g(cuda_device):
     c = native.rbf_backward(X, Y, G1 + 2 * G2, K, 1 / 64, workspace=ws)
     for u, v, w in zip(a, b, c):
         torch.testing.assert_close(w, u + 2 * v, atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize("case", ["rbf", "cosine_sim"])
+def test_backward_repeatable_at_8192(case, cuda_device):
+    """30 backward passes at N = M = 8192 agree with the first to fp32 rounding (the atomic
+    flushes reorder sums, nothing more).  Guards the pipeline's buffer hand-offs: a stage reused
+    before every lane had read it showed up here as a wrong block of rows in a few runs of 30."""
+    from cases.cosine_sim import native as cn
+    from cases.rbf import native
+    gen = torch.Generator(device="cuda").manual_seed(8192)
+    N = M = 8192
+    X = torch.randn(N, 64, device="cuda", generator=gen)
+    Y = torch.randn(M, 64, device="cuda", generator=gen)
+    G = torch.randn(N, M, device="cuda", generator=gen)
+    if case == "rbf":
+        K, ws = native.forward_with_workspace(X, Y, 1 / 64)
+        run = lambda: native.rbf_backward(X, Y, G, K, 1 / 64, workspace=ws)  # noqa: E731
+    else:
+        _, ws = cn.forward_with_workspace(X, Y, 1e-8)
+        run = lambda: cn.cos_backward(G, N, M, 64, 1e-8, workspace=ws)  # noqa: E731
+    first = [t.clone() for t in run()]
+    for _ in range(30):
+        for u, v in zip(run(), first):
+            torch.testing.assert_close(u, v, rtol=1e-4, atol=1e-5)
+    assert native.read_status(ws) == 0
