@@ -40,7 +40,8 @@
 // TMEM (512 columns): [0,64) dY acc | [64,128) dX acc | [128,256) two W buffers (hi 32 + lo
 // 32) | [256,384) W^T hi (128 columns of i) | [384,512) W^T lo.
 // Shared memory (DS = 64): strip ring 4 x 32 KiB, X ring 2 x 16 KiB, Y ring 2 x 16 KiB, dX
-// staging 4 x 8 KiB.
+// staging 4 x 8 KiB.  (Build option RBF_BWD_XSTAGES=4: X ring 4 x 16 KiB, no staging; measured
+// slower.)
 // Warps: 0 TMA producer of strips + Y rows, 1 TMA producer of X rows, 2 dY MMA issuer, 3 dX MMA
 // issuer, 4-7 C-warps, 8-11 R-warps (warp w reaches TMEM lanes 32*(w%4)..+31).  Independent
 // pipelines sit in different warps: a lane blocked in mbarrier.try_wait holds back its whole
@@ -60,7 +61,13 @@ namespace {
 constexpr int BT = 128;        // tile edge (rows of i and columns of j)
 constexpr int SR = 32;         // strip width
 constexpr int STAGES = 4;      // strip ring: one stage per strip of a tile
-constexpr int XSTAGES = 2;     // X-row ring
+#ifndef RBF_BWD_XSTAGES
+#define RBF_BWD_XSTAGES 2
+#endif
+// X-row ring.  At 4 stages the dX flush staging gives up its shared memory (dX is then flushed
+// with red.add from registers, c * rowsum * x included, and no finalize pass runs).
+constexpr int XSTAGES = RBF_BWD_XSTAGES;
+constexpr bool kStageDx = XSTAGES <= 2;
 constexpr int YSTAGES = 2;     // Y-row ring
 constexpr int THREADS = 384;
 constexpr uint32_t BOX = 32 * 32 * 4;       // 32x32 fp32, 4 KiB
@@ -75,7 +82,7 @@ struct Cfg {
   static constexpr uint32_t X_BYTES = (DS / 32) * BOX;   // 32 rows x DS features, hi or lo
   static constexpr uint32_t STAGING = X_BYTES;           // one R-warp's dX flush: 32 x DS
   static constexpr size_t SMEM = 1024 + STAGES * 2 * STRIP + XSTAGES * 2 * X_BYTES +
-                                 YSTAGES * 2 * X_BYTES + 4 * STAGING + 512;
+                                 YSTAGES * 2 * X_BYTES + (kStageDx ? 4 : 0) * STAGING + 512;
 };
 static_assert(Cfg<64>::SMEM <= 232448, "backward shared memory over the sm_100 limit");
 
@@ -273,12 +280,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* xring = ring + STAGES * 2 * STRIP;           // [XSTAGES][X hi | X lo]
   uint8_t* yring = xring + XSTAGES * 2 * C::X_BYTES;    // [YSTAGES][Y hi | Y lo]
   uint8_t* staging = yring + YSTAGES * 2 * C::X_BYTES;  // [4 R-warps][32 rows x DS]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(staging + 4 * C::STAGING);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(staging + (kStageDx ? 4 : 0) * C::STAGING);
   uint64_t* full = bar;              // [4] strip landed            TMA -> R-warps, C-warp
   uint64_t* empty = full + 4;        // [4] strip consumed          R-warps, C-warp -> TMA
-  uint64_t* xfull = empty + 4;       // [2] X rows landed           TMA -> dY issuer
-  uint64_t* xempty = xfull + 2;      // [2] X rows consumed         dY issuer -> TMA
-  uint64_t* yfull = xempty + 2;      // [2] Y rows landed           TMA -> dX issuer
+  uint64_t* xfull = empty + 4;       // [XSTAGES] X rows landed     TMA -> dY issuer
+  uint64_t* xempty = xfull + XSTAGES;  // [XSTAGES] X rows consumed dY issuer -> TMA
+  uint64_t* yfull = xempty + XSTAGES;  // [2] Y rows landed         TMA -> dX issuer
   uint64_t* yempty = yfull + 2;      // [2] Y rows consumed         dX issuer -> TMA
   uint64_t* w_full = yempty + 2;     // [2] W buffer written        R-warps -> dX issuer
   uint64_t* w_empty = w_full + 2;    // [2] W buffer read           dX issuer -> R-warps
@@ -302,9 +309,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], 5);  // 4 R-warps + the C-warp of this quadrant
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < XSTAGES; ++s) {
       ptx::mbar_init(&xfull[s], 1);
       ptx::mbar_init(&xempty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       ptx::mbar_init(&yfull[s], 1);
       ptx::mbar_init(&yempty[s], 1);
       ptx::mbar_init(&w_full[s], 4);
@@ -517,7 +526,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       if (!ok)
-        for (int s = 0; s < 2; ++s)
+        for (int s = 0; s < XSTAGES; ++s)
           if (xissued >> s & 1u) ptx::mbar_wait_bounded(&xfull[s], bit_of(xlast, s), a.status, a.timeout_ns);
     }
   } else if (warp == 2 || warp == 3) {
@@ -925,7 +934,7 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
   const bool dot = epi == Epi::kDot;
   const bool routed = route != nullptr && route->world > 0;
   const PrepLayout L = prep_layout(N, M, D);
-  const bool tma_flush = (D % 4) == 0;  // dX rows 16-byte pitched
+  const bool tma_flush = kStageDx && (D % 4) == 0;  // dX rows 16-byte pitched, staging present
   float* rowsum = ws_at<float>(ws, L.end);
   int* counter = ws_at<int>(ws, L.end + rowsum_bytes(N));
   const bool work = N > 0 && M > 0 && D > 0;
