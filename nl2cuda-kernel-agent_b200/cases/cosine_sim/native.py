@@ -51,7 +51,7 @@ def workspace_bytes(N, M, D):
 
 
 def _shapes(A, B):
-    _rbf._check_2d(("A", "B"), (A, B))
+    _rbf.check_2d(("A", "B"), (A, B))
     if A.size(1) != B.size(1):
         raise RuntimeError("A, B must share feature dim D")
     if A.device != B.device:
@@ -61,15 +61,15 @@ def _shapes(A, B):
 def forward_with_workspace(A, B, eps):
     """S and the filled workspace (normalised rows and norms, reused by the backward)."""
     _shapes(A, B)
-    A, B = _rbf._operand(A), _rbf._operand(B)
+    A, B = _rbf.operand(A), _rbf.operand(B)
     N, D = A.shape
     M = B.size(0)
     with torch.cuda.device(A.device):
         S = torch.empty((N, M), dtype=torch.float32, device=A.device)
         ws = torch.empty(workspace_bytes(N, M, D), dtype=torch.uint8, device=A.device)
-        _rbf.check(lib().cos_sm100_forward(_rbf._ptr(A), _rbf._ptr(B), _rbf._ptr(S), N, M, D,
-                                           float(eps), _rbf._ptr(ws), ws.numel(),
-                                           _rbf._stream(A.device)), "cos_sm100_forward")
+        _rbf.check(lib().cos_sm100_forward(_rbf.ptr(A), _rbf.ptr(B), _rbf.ptr(S), N, M, D,
+                                           float(eps), _rbf.ptr(ws), ws.numel(),
+                                           _rbf.stream_of(A.device)), "cos_sm100_forward")
     return S, ws
 
 
@@ -81,26 +81,26 @@ def cos_forward(A, B, eps):
 def cos_backward(dS, N, M, D, eps, workspace=None, A=None, B=None):
     """[dA, dB] of sum(dS * S).  ``workspace`` from ``forward_with_workspace`` of the same A, B
     (``cos_sm100_backward_prepared``), or else A and B (``cos_sm100_backward``)."""
-    _rbf._check_2d(("dS",), (dS,))
+    _rbf.check_2d(("dS",), (dS,))
     if tuple(dS.shape) != (N, M):
         raise RuntimeError("shape mismatch: dS must be [N, M]")
-    dS = _rbf._operand(dS)
+    dS = _rbf.operand(dS)
     dev = dS.device
     with torch.cuda.device(dev):
         dA = torch.empty((N, D), dtype=torch.float32, device=dev)
         dB = torch.empty((M, D), dtype=torch.float32, device=dev)
         if workspace is not None:
             _rbf.check(lib().cos_sm100_backward_prepared(
-                _rbf._ptr(dS), _rbf._ptr(dA), _rbf._ptr(dB), N, M, D, float(eps),
-                _rbf._ptr(workspace), workspace.numel(), _rbf._stream(dev)),
+                _rbf.ptr(dS), _rbf.ptr(dA), _rbf.ptr(dB), N, M, D, float(eps),
+                _rbf.ptr(workspace), workspace.numel(), _rbf.stream_of(dev)),
                 "cos_sm100_backward_prepared")
         else:
             if A is None or B is None:
                 raise RuntimeError("cos_backward needs the forward's workspace, or A and B")
             _shapes(A, B)
-            A, B = _rbf._operand(A), _rbf._operand(B)
+            A, B = _rbf.operand(A), _rbf.operand(B)
             ws = torch.empty(workspace_bytes(N, M, D), dtype=torch.uint8, device=dev)
             _rbf.check(lib().cos_sm100_backward(
-                _rbf._ptr(A), _rbf._ptr(B), _rbf._ptr(dS), _rbf._ptr(dA), _rbf._ptr(dB), N, M, D,
-                float(eps), _rbf._ptr(ws), ws.numel(), _rbf._stream(dev)), "cos_sm100_backward")
+                _rbf.ptr(A), _rbf.ptr(B), _rbf.ptr(dS), _rbf.ptr(dA), _rbf.ptr(dB), N, M, D,
+                float(eps), _rbf.ptr(ws), ws.numel(), _rbf.stream_of(dev)), "cos_sm100_backward")
     return [dA, dB]

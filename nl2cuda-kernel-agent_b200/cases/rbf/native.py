@@ -151,6 +151,13 @@ def rbf_backward(X, Y, G, K, gamma, workspace=None, entry="rbf_sm100_backward"):
     return [dX, dY]
 
 
+# The ctypes helpers above, shared with the other case bound to this library (cosine_sim).
+check_2d = _check_2d
+operand = _operand
+ptr = _ptr
+stream_of = _stream
+
+
 def launch_count():
     """Kernels this library has enqueued in this process."""
     return int(lib().rbf_sm100_launch_count())
