@@ -52,3 +52,19 @@ def test_profile_candidate_sees_the_library_kernels(cuda_device):
     table, cuda_us, wall_us = profile.profile_candidate("rbf", mode="both", iters=3)
     assert "rbf_fwd_tc_kernel" in table and "rbf_bwd_tc_kernel" in table
     assert 0 < cuda_us and 0 < wall_us
+
+
+def test_timeline_formatting():
+    import numpy as np
+    from framework.timeline import ROLES, format_timeline
+    buf = np.zeros((8, 1024), np.uint64)
+    n = np.zeros(8, np.int32)
+    t0 = 5_000_000
+    buf[0][0] = (10 << 56) | t0
+    buf[0][1] = (11 << 56) | (t0 + 640)
+    buf[4][0] = (30 << 56) | (t0 + 1500)
+    n[0], n[4] = 2, 1
+    lines = format_timeline(buf, n)
+    assert lines == ["PROD 10@0.00 11@0.64", "C0 30@1.50"]
+    assert format_timeline(np.zeros((8, 4), np.uint64), np.zeros(8, np.int32)) == []
+    assert len(ROLES) == 8
