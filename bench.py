@@ -488,13 +488,13 @@ def run_cosine(args):
     from cases.cosine_sim import native as cnative
     from cases.cosine_sim import op as cop
     from cases.rbf import native
-    from oracle import reference_port
 
     n = M = args.cos_size
     D, eps = 64, cos_config.EPS
     metric = COS_METRIC.format(n=n)
     workload_name = f"cosine_sim fwd+bwd fp32, N=M={n}, D={D}, eps={eps:g}"
     if args.impl == "reference":
+        from oracle import reference_port
         threads = os.cpu_count() or 1
         sec, done = reference_port.cos_time_sample(n, M, D, eps, 256, threads,
                                                    min_seconds=max(1.0, args.cpu_seconds / 4))
@@ -632,6 +632,7 @@ def run_cosine(args):
 
     cpu = None
     if not args.no_cpu_baseline:
+        from oracle import reference_port
         threads = os.cpu_count() or 1
         sec, done = reference_port.cos_time_sample(n, M, D, eps, 512, threads,
                                                    min_seconds=0.75 * args.cpu_seconds)
