@@ -522,14 +522,14 @@ def run_cosine(args):
     def fwd():
         return cnative.forward_with_workspace(A, B, eps)
 
-    S, ws = fwd()
+    _, ws = fwd()  # the workspace the backward graph reads
 
     def bwd():
         return cnative.cos_backward(dS, n, M, D, eps, workspace=ws)
 
     def step_fb():
-        S_, ws_ = cnative.forward_with_workspace(A, B, eps)
-        cnative.cos_backward(dS, n, M, D, eps, workspace=ws_)
+        _, ws_step = cnative.forward_with_workspace(A, B, eps)
+        cnative.cos_backward(dS, n, M, D, eps, workspace=ws_step)
 
     for _ in range(max(args.warmup, 0)):
         step_fb()
