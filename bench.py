@@ -7,13 +7,18 @@ gradient G, fp32 in and out.  FLOP per step = 6*N*M*D; algorithmic HBM bytes per
 12*N*M + 12*(N+M)*D.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c1]
+                  [--scaling weak|strong]
 
-N = 1 runs config c1 (N=M=4096, D=64).  Under torchrun (WORLD_SIZE = N > 1) the work is
-weak-scaled by rows: every rank owns 4096 rows of X (and of G, K), Y (4096 x 64) is replicated,
-and the partial dY is reduced inside the backward over NVLink peer memory (the dY partials go
-straight into the owning rank's buffer, then one bounded cross-GPU barrier and a gather) up to 4
-ranks, and with one NCCL all-reduce beyond, where that measured faster (RBF_DY_REDUCE=peer or
-nccl forces either) ("scaling": "weak").
+N = 1 runs config c1 (N=M=4096, D=64); --config c0..c4 picks another BASELINE configuration.
+Under torchrun (WORLD_SIZE = N > 1) the work is sharded by rows of X (and of G, K) with Y
+replicated.  --scaling weak (the default): every rank owns the config's N rows ("scaling":
+"weak").  --scaling strong: the config's N rows are split across the ranks, so the same problem
+is solved at every N (the c4 1->8 GPU target: --config c4 --scaling strong).  The partial dY is
+reduced over NVLink peer memory by this library (the dY partials go into the rank's slot of a
+symmetric buffer, then one bounded cross-GPU barrier and a gather) up to 4 ranks while dY is
+small, and with one NCCL all-reduce otherwise, where that measured faster (RBF_DY_REDUCE=peer or
+nccl forces either).  After timing, every rank checks sampled rows of K and dX and columns of dY
+of one more step against the CPU oracle ("parity" in the JSON line).
 ``value`` = whole-job GFLOP/s = (6 * N_global * M * D) / (max over ranks of the device time of
 one step).  Inputs are resident in HBM when timing starts; L2 is flushed before every timed
 step, outside the events: a 256 MiB write, then a 256 MiB read of a second buffer, so that the
@@ -51,7 +56,12 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--config", default="c1")
+    ap.add_argument("--config", default="c1", help="c0..c4 (cases/rbf/config.py CONFIGS)")
+    ap.add_argument("--scaling", choices=("weak", "strong"), default="weak",
+                    help="weak: every rank owns the config's N rows (N_global = N * world); "
+                         "strong: the config's N rows are split across the ranks")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the post-timing oracle spot check of sampled rows / columns")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -224,52 +234,84 @@ def nvsmi_id(device):
         return device.index if device.index is not None else 0
 
 
-def workload(cfg_name, world):
+def workload(cfg_name, world, rank=0, scaling="weak"):
+    """The config's shapes and this rank's rows.  weak: every rank owns N rows (N_global =
+    N * world); strong: the config's N rows are split by shard.row_range."""
     from cases.rbf import config
     c = dict(config.CONFIGS[cfg_name])
-    c["rows_per_rank"] = c["N"]
-    c["N_global"] = c["N"] * world
+    if scaling == "strong":
+        from cases.rbf import shard
+        c["N_global"] = c["N"]
+        c["row0"], row1 = shard.row_range(c["N"], world, rank)
+        c["rows_per_rank"] = row1 - c["row0"]
+    else:
+        c["N_global"] = c["N"] * world
+        c["row0"] = rank * c["N"]
+        c["rows_per_rank"] = c["N"]
     return c
 
 
 def run_reference(args, world, rank):
-    """The reference's CPU implementation (oracle/reference_port.py) on this host's cores."""
+    """The reference's CPU implementation (oracle/reference_port.py) on this host's cores.
+
+    Where the whole workload fits (the [N, M, D] broadcast intermediate of reference.py and its
+    autograd buffers within a third of the available host memory, and one step within ~20 s of
+    CPU time, e.g. c0 and c1 on a many-core host) every step is the reference's forward +
+    backward over ALL rows, as written.  Otherwise a step is a bounded sample of rows of X
+    against all of Y, and ms_per_step scales it linearly to all N rows."""
     if rank != 0:
         return
     import torch
     from oracle import reference_port
-    c = workload(args.config, world)
+    c = workload(args.config, world, 0, args.scaling)
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     N, M, D, g = c["N_global"], c["M"], c["D"], c["gamma"]
-    # One step = a bounded sample of rows of X against all of Y, sized to ~1 s of CPU work.
     probe_s, probe_rows = reference_port.time_sample(N, M, D, g, 32, threads)
-    rows = int(max(8, min(N, 32 * max(1.0, 1.0 / max(probe_s, 1e-3)))))
+    per_row_s = probe_s / max(probe_rows, 1)
+    try:
+        import psutil
+        avail = psutil.virtual_memory().available
+    except Exception:  # pragma: no cover
+        avail = 0
+    full_bytes = 4 * 4 * N * M * D  # diff, diff**2 and their autograd grads, fp32
+    verbatim = full_bytes < avail / 3 and per_row_s * N < 20.0
+    if verbatim:
+        rows = N
+    else:
+        # One step = a bounded sample of rows of X against all of Y, ~1 s of CPU work.
+        rows = int(max(8, min(N, 32 * max(1.0, 1.0 / max(probe_s, 1e-3)))))
     gen = torch.Generator().manual_seed(0)
     X = torch.randn(rows, D, generator=gen)
     Y = torch.randn(M, D, generator=gen)
     G = torch.randn(rows, M, generator=gen)
+    block = rows if verbatim else 256
     for _ in range(args.warmup):
-        reference_port.forward_backward(X, Y, G, g)
+        reference_port.forward_backward(X, Y, G, g, block_rows=block)
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        reference_port.forward_backward(X, Y, G, g)
+        reference_port.forward_backward(X, Y, G, g, block_rows=block)
         times.append(time.perf_counter() - t0)
     per_row = statistics.mean(times) / rows
-    ms_step = per_row * N * 1e3  # extrapolated to the full workload (linear in rows)
+    ms_step = per_row * N * 1e3
     gflops = 6.0 * rows * M * D / statistics.mean(times) / 1e9
+    if verbatim:
+        sample = f"all {N} rows of X x all {M} rows of Y, fwd+bwd, per step (reference.py as written)"
+        extrap = "none: every step runs the whole workload"
+    else:
+        sample = f"{rows} rows of X x all {M} rows of Y, fwd+bwd, per step"
+        extrap = "ms_per_step scales the sample linearly to all N rows"
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gflops, 3), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_step, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"{args.config}: RBF fwd+bwd N={N} M={M} D={D} gamma={g:.6g}",
                    "N": N, "M": M, "D": D, "sample_rows_per_step": rows,
-                   "extrapolation": "ms_per_step scales the sample linearly to all N rows"},
+                   "extrapolation": extrap},
         "cpu_baseline": {"value": round(gflops, 3), "unit": UNIT, "cores": threads,
-                         "kind": "port",
-                         "sample": f"{rows} rows of X x all {M} rows of Y, fwd+bwd, per step"},
+                         "kind": "port", "sample": sample},
         "e2e": {"value": round(gflops, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -315,13 +357,15 @@ def main():
     dev = torch.device("cuda", local_rank)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
-    c = workload(args.config, world)
+    c = workload(args.config, world, rank, args.scaling)
     n, M, D, g = c["rows_per_rank"], c["M"], c["D"], c["gamma"]
-    Ng = c["N_global"]
+    Ng, row0 = c["N_global"], c["row0"]
 
-    # Inputs: this rank's rows of X (and of G), Y replicated; resident in HBM.
-    X_all, Y = draw(1234, torch.float32, dev, n * world, M, D, c["ydist"], c["xscale"])
-    X = X_all[rank * n:(rank + 1) * n].contiguous()
+    # Inputs: this rank's rows of X (and of G), Y replicated; resident in HBM.  X is drawn for
+    # all N_global rows from one seed, so a strong-scaling run at any world size solves the
+    # same X, Y.
+    X_all, Y = draw(1234, torch.float32, dev, Ng, M, D, c["ydist"], c["xscale"])
+    X = X_all[row0:row0 + n].contiguous()
     del X_all
     G = torch.randn(n, M, dtype=torch.float32, device=dev,
                     generator=torch.Generator(device=dev).manual_seed(777 + rank))
@@ -333,9 +377,11 @@ def main():
         # auto: the library's NVLink peer exchange up to 4 ranks, where it measured faster than
         # NCCL (109.5 vs 115.5 us per step at 2 GPUs, 115.7 vs 119.2 at 4); NCCL at 8 (129.5 vs
         # 133.5 us: every rank then reads 7 MB of partials).
+        # A large dY (c4: 64 MB) goes to NCCL at every N: the one-phase peer sum reads every
+        # rank's whole partial.
         dy_reduce = os.environ.get("RBF_DY_REDUCE", "auto")
         if dy_reduce == "auto":
-            dy_reduce = "peer" if world <= 4 else "nccl"
+            dy_reduce = "peer" if world <= 4 and M * D * 4 <= (8 << 20) else "nccl"
         if dy_reduce == "peer":
             route = shard.RoutedDy(M, D, dev)
 
@@ -430,10 +476,23 @@ def main():
     t_roof = max(t_tc, t_hbm)
     gflops = flop / (ms * 1e-3) / 1e9
 
-    # End to end through the public API with host buffers.
-    e2e = None
-    if not args.no_e2e:
+    # End to end through the public API with host buffers (skipped where one step would copy
+    # more than 4 GiB over PCIe: c2-c4 move 2-32 GiB of K and G per step, which the host link,
+    # not the kernels, would time).
+    e2e, e2e_skipped = None, None
+    if args.no_e2e:
+        e2e_skipped = "--no-e2e"
+    elif 8 * n * M > (4 << 30):
+        e2e_skipped = f"host copies of {8 * n * M / 2**30:.1f} GiB per step (K out, G in)"
+    else:
         e2e = run_e2e(X, Y, G, g, world, dev, args, shard, op, route)
+
+    # Parity of this very run, after timing: sampled K and dX rows of every rank, and dY
+    # columns (each rank's fp64 oracle partial over its rows, summed across ranks) against the
+    # CPU oracle under the 1e-3 gate.  The oracle is imported only here.
+    parity = None
+    if not args.no_parity:
+        parity = spot_check(X, Y, G, g, step, world, dev, shard)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -443,10 +502,12 @@ def main():
         line = {
             "metric": METRIC, "value": round(gflops, 2), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
+            "dtype": "f32",
             "data": "synthetic (seeded X, Y, G with the config's distributions)",
             "config": {"workload": f"{args.config}: RBF fwd+bwd fp32, {n} rows of X per rank "
-                                   f"(N={Ng} total), M={M}, D={D}, gamma={g:.6g}",
+                                   f"(N={Ng} total, {args.scaling} scaling), M={M}, D={D}, "
+                                   f"gamma={g:.6g}",
                        "N": Ng, "M": M, "D": D, "rows_per_rank": n,
                        "l2": "flushed before every timed step (256 MiB write + 256 MiB read, outside events)",
                        "parallelism": f"row-shard x{world}" + (
@@ -461,7 +522,10 @@ def main():
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "parity": parity,
         }
+        if e2e_skipped:
+            line["e2e_skipped"] = e2e_skipped
         print(json.dumps(line), flush=True)
     # Graphs that captured NCCL work must be gone before the communicator is; the process then
     # exits without tearing the process group down (destroying it while captured collectives
@@ -473,6 +537,48 @@ def main():
         sys.stdout.flush()
         sys.stderr.flush()
         os._exit(0)
+
+
+def spot_check(X, Y, G, gamma, step, world, dev, shard, n_rows=8, n_cols=8, seed=5):
+    """Max errors of one untimed step against the CPU oracle on sampled rows / columns."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from oracle import oracle
+    K, dX, dY = step()
+    torch.cuda.synchronize()
+    n, M = G.shape
+    rng = np.random.default_rng(seed)
+    rows = np.unique(np.concatenate([[0, n - 1], rng.integers(0, n, n_rows)])) if n else \
+        np.zeros(0, np.int64)
+    cols = np.unique(np.concatenate([[0, M - 1], rng.integers(0, M, n_cols)]))
+    ri = torch.from_numpy(rows).to(dev)
+    ci = torch.from_numpy(cols).to(dev)
+    Xh, Yh = X.cpu().numpy(), Y.cpu().numpy()
+    k_ref = oracle.forward_rows(Xh, Yh, gamma, rows)
+    dx_ref = oracle.dx_rows(Xh[rows], Yh, G.index_select(0, ri).cpu().numpy(), gamma,
+                            np.arange(len(rows)))
+    dy_part = oracle.dy_cols(Xh, Yh[cols], G.index_select(1, ci).cpu().numpy(), gamma,
+                             np.arange(len(cols)))
+    dy_ref = torch.from_numpy(dy_part).to(dev)
+    if world > 1:
+        dist.all_reduce(dy_ref)  # fp64 sum of every rank's oracle partial
+    dy_ref = dy_ref.cpu().numpy()
+    out = {}
+    ok = True
+    for name, got, ref in (("K", K.index_select(0, ri).cpu().numpy(), k_ref),
+                           ("dX", dX.index_select(0, ri).cpu().numpy(), dx_ref),
+                           ("dY", dY.index_select(0, ci).cpu().numpy(), dy_ref)):
+        err = np.abs(got.astype(np.float64) - ref)
+        mabs = float(err.max()) if err.size else 0.0
+        mrel = float((err / np.maximum(np.abs(ref), 1e-6)).max()) if err.size else 0.0
+        ok = ok and bool(np.all(err <= 1e-3 + 1e-3 * np.abs(ref)))
+        out[name] = [shard.max_over_ranks(mabs, device=dev), shard.max_over_ranks(mrel, device=dev)]
+    ok = shard.max_over_ranks(0.0 if ok else 1.0, device=dev) == 0.0
+    return {"max_abs": max(v[0] for v in out.values()),
+            "per_output_max_abs_rel": out, "gate_1e-3": ok,
+            "sample": f"{len(rows)} rows of K and dX per rank, {len(cols)} columns of dY, "
+                      "vs the fp64 CPU oracle, after timing"}
 
 
 COS_METRIC = "cosine_sim fwd+bwd GFLOP/s at N=M={n} D=64 (one GPU)"

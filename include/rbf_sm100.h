@@ -135,10 +135,12 @@ RBF_API int rbf_sm100_backward_shard_routed(const float* X_local, const float* Y
  * j-block (j-block % world) sums it over every rank's slot; barrier; the full dY [M, D] is
  * gathered from the owners; *step_counter advances (device int, 0 on every rank before the first
  * step).  Both barriers are bounded by RBF_WAIT_TIMEOUT_MS: on expiry the workspace status word
- * reads RBF_ERR_TIMEOUT, dY is not written and the buffers must be set up again.
- * `flag_arrays[r]`: rank r's int[world] signal array (peer memory, zeroed once); `tickets`: two
- * zeroed device unsigned ints of this rank.  D % 4 == 0.  No host synchronisation, so a captured
- * CUDA graph of the step can be replayed. */
+ * reads RBF_ERR_TIMEOUT, dY is not written, the step counter does not advance, and tickets[2]
+ * is set: every later exchange on these buffers then skips its work and reports
+ * RBF_ERR_TIMEOUT, until the caller sets the buffers up again (flags, counter and tickets
+ * zeroed on every rank).  `flag_arrays[r]`: rank r's int[world] signal array (peer memory,
+ * zeroed once); `tickets`: three zeroed device unsigned ints of this rank.  D % 4 == 0.  No host
+ * synchronisation, so a captured CUDA graph of the step can be replayed. */
 RBF_API int rbf_sm100_dy_exchange(float* dY, int64_t M, int64_t D, float* const* dy_buffers,
                                   int* const* flag_arrays, int world, int rank, int* step_counter,
                                   unsigned* tickets, void* workspace, size_t workspace_bytes,
@@ -157,15 +159,22 @@ RBF_API int rbf_sm100_read_status(void* workspace, rbf_stream_t stream, int* dev
  * until the process exits).  The caller still passes X, Y and K.  Calls whose workspace would
  * exceed the capacity return RBF_ERR_TOO_LARGE (about (N+M)*(2*Dp+1)*4 bytes are needed,
  * Dp = D rounded up to 32; e.g. N = M = 4096 at D = 64 fits).  Allocates nothing: no cudaMalloc,
- * no cudaFree, no allocating library call.  The first call on each device looks up the
- * array's device address with that device current (cudaGetSymbolAddress); make that first
- * call before any stream capture.  All calls share the one array, so calls that overlap on the
- * GPU (different streams, or other host threads) race and must be serialised by the caller.
+ * no cudaFree, no allocating library call.  The first call in each CUDA context looks up the
+ * array's device address with that context current (cudaGetSymbolAddress) and caches it per
+ * context; make that first call before any stream capture.  All calls share the one array, so
+ * calls that overlap on the GPU (different streams, or other host threads) race and must be
+ * serialised by the caller.  A device-side wait that ran out (RBF_ERR_TIMEOUT: K is then only
+ * partly written) is reported by rbf_sm100_forward_noalloc_read_status, which reads the array's
+ * status word; the next call resets it.
  * ------------------------------------------------------------------------------------------- */
 RBF_API size_t rbf_sm100_forward_noalloc_capacity(void);
 RBF_API int rbf_sm100_forward_noalloc(const float* X, const float* Y, float* K,
                                       int64_t N, int64_t M, int64_t D, float gamma,
                                       rbf_stream_t stream);
+/* Status word of the allocation-free forward's internal array: RBF_OK, or RBF_ERR_TIMEOUT when a
+ * device-side wait of the last call ran out.  Blocking, like rbf_sm100_read_status (synchronizes
+ * `stream`, copies the word to the host with a plain cudaMemcpy, resets it); allocates nothing. */
+RBF_API int rbf_sm100_forward_noalloc_read_status(rbf_stream_t stream, int* device_status);
 
 /* ---------------------------------------------------------------------------------------------
  * Legacy host-pointer ABI of the reference's standalone delivery

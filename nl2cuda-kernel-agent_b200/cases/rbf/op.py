@@ -6,7 +6,7 @@ also saves the workspace holding the TF32 split of X and Y, so the backward skip
 """
 import torch
 
-from cases.rbf import native
+from cases.rbf import native, shard
 
 
 class RBFFunction(torch.autograd.Function):
@@ -22,6 +22,14 @@ class RBFFunction(torch.autograd.Function):
     def backward(ctx, G):
         X, Y, K = ctx.saved_tensors
         dX, dY = native.rbf_backward(X, Y, G.contiguous(), K, ctx.gamma, workspace=ctx.workspace)
+        if shard.check_status_default():
+            # RBF_CHECK_STATUS=1: one synchronisation per step, so that a bounded device wait
+            # that ran out (in the forward or this backward) raises instead of returning partial
+            # gradients.
+            st = native.read_status(ctx.workspace)
+            if st != 0:
+                raise RuntimeError(f"rbf backward: device status {st} (a bounded device-side "
+                                   "wait timed out)")
         ctx.workspace = None
         return dX, dY, None
 

@@ -11,8 +11,18 @@ gloo on CPU in the tests) or, with ``RoutedDy``, fused into the backward over pe
 compute is pluggable so that the same driver runs with the sm_100a kernels (``native``) or with
 a CPU implementation in tests.
 """
+import os
+
 import torch
 import torch.distributed as dist
+
+RBF_ERR_TIMEOUT = 7
+
+
+def check_status_default():
+    """RBF_CHECK_STATUS=1 makes the production paths read the device status word after every
+    step (one host synchronisation per step) and raise on a timed-out device wait."""
+    return os.environ.get("RBF_CHECK_STATUS", "0") not in ("", "0")
 
 
 def row_range(n_rows, world, rank):
@@ -33,6 +43,11 @@ class NativeShardCompute:
     def backward(self, X, Y, G, K, gamma, state):
         from cases.rbf import native
         return native.rbf_backward(X, Y, G, K, gamma, workspace=state)
+
+    def status(self, state):
+        """Device status word of the step's workspace (0 ok, 7 a bounded wait ran out)."""
+        from cases.rbf import native
+        return native.read_status(state)
 
 
 class RoutedDy:
@@ -66,27 +81,51 @@ class RoutedDy:
             self.counters = torch.zeros(4, dtype=torch.int32, device=self.device)
             torch.cuda.synchronize()
         self.handle = symm_mem.rendezvous(self.buffer, group)
+        # counters: [step, ticket 0, ticket 1, sticky failure flag] (rbf_sm100_dy_exchange)
         ptrs = [int(p) for p in self.handle.buffer_ptrs]
         self.dy_ptrs = (ctypes.c_void_p * self.world)(*ptrs)
         self.flag_ptrs = (ctypes.c_void_p * self.world)(*[p + self.flags_offset for p in ptrs])
         dist.barrier(group=group)  # every rank's slots and flags are zero before the first step
 
+    def failed(self):
+        """True once an exchange on these buffers timed out (a peer never arrived): every later
+        exchange skips its work, and the buffers must be built again.  Synchronizes."""
+        return int(self.counters[3].item()) != 0
+
+
+def _raise_on_status(st, where):
+    if st != 0:
+        raise RuntimeError(f"{where}: device status {st}"
+                           + (" (a bounded device-side wait timed out; K, dX or dY are incomplete)"
+                              if st == RBF_ERR_TIMEOUT else ""))
+
 
 def forward_backward_shard(X_local, Y, G_local, gamma, compute=None, group=None,
-                           reduce_dy=True, route=None):
+                           reduce_dy=True, route=None, check_status=None):
     """One forward + backward of this rank's rows.  Returns (K_local, dX_local, dY) where dY is
     the full gradient when ``reduce_dy`` and the process group is initialised (all-reduced over
     ``group`` with NCCL, or -- with ``route``, a ``RoutedDy`` -- reduced inside the backward
-    over peer memory), else this rank's partial sum."""
+    over peer memory), else this rank's partial sum.
+
+    ``check_status`` (default: RBF_CHECK_STATUS=1): after the step, read the device status word
+    (one synchronisation) and raise RuntimeError if a bounded device wait ran out -- in the
+    forward, the backward or the dY exchange (whose timeout is sticky: later steps on the same
+    ``route`` raise too, until it is built again)."""
     compute = compute or NativeShardCompute()
+    if check_status is None:
+        check_status = check_status_default()
     if route is not None:
         from cases.rbf import native
         K_local, ws = native.forward_with_workspace(X_local, Y, gamma)
         dX_local = native.rbf_backward_shard_routed(X_local, Y, G_local, K_local, gamma, ws, route)
         dY = native.dy_exchange(route, ws)
+        if check_status:
+            _raise_on_status(native.read_status(ws), "routed row-sharded step")
         return K_local, dX_local, dY
     K_local, state = compute.forward(X_local, Y, gamma)
     dX_local, dY = compute.backward(X_local, Y, G_local, K_local, gamma, state)
+    if check_status and hasattr(compute, "status"):
+        _raise_on_status(compute.status(state), "row-sharded step")
     if reduce_dy and dist.is_available() and dist.is_initialized():
         dist.all_reduce(dY, op=dist.ReduceOp.SUM, group=group)
     return K_local, dX_local, dY

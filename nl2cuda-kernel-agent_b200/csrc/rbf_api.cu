@@ -470,25 +470,66 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
-// Device address of g_noalloc_scratch for the current device, looked up once per device.  In
+// The current driver context (cuCtxGetCurrent, reached through the runtime's driver entry-point
+// table so that the library does not link libcuda directly).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<CtxGetCurrentFn>(nullptr);
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  return fn;
+}
+
+// Device address of g_noalloc_scratch in the current context, looked up once per context.  In
 // host code the array's name is only a stand-in, never a device address, so the address must
-// come from cudaGetSymbolAddress with that device current.
+// come from cudaGetSymbolAddress with that device current.  The cache is keyed by the driver
+// context, not the device ordinal: a caller that runs its own (non-primary) context, or that
+// reset the device, gets the address that belongs to the context it is using.
 int noalloc_scratch(void** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_detail(RBF_ERR_NO_DEVICE, "cudaGetDevice", e);
-  static std::mutex mu;
-  static void* addr[64] = {};
-  std::lock_guard<std::mutex> lock(mu);
-  if (dev < 0 || dev >= 64) return set_detail(RBF_ERR_NO_DEVICE, "device ordinal >= 64");
-  if (addr[dev] == nullptr) {
+  CtxGetCurrentFn get = ctx_get_current();
+  CUcontext ctx = nullptr;
+  if (get == nullptr || get(&ctx) != CUDA_SUCCESS)
+    return set_detail(RBF_ERR_NO_DEVICE, "cuCtxGetCurrent");
+  if (ctx == nullptr) {
+    // No context bound to this thread yet: the runtime binds the primary context of `dev` on its
+    // first call that needs one (this lookup), then the context is read again.
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr)
+    if ((e = cudaGetSymbolAddress(&p, g_noalloc_scratch)) != cudaSuccess)
       return set_detail(RBF_ERR_CUDA, "cudaGetSymbolAddress(scratch)", e);
-    addr[dev] = p;
+    if (get(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+      return set_detail(RBF_ERR_NO_DEVICE, "no current CUDA context");
   }
-  *out = addr[dev];
+  static std::mutex mu;
+  constexpr int kSlots = 64;
+  static CUcontext keys[kSlots] = {};
+  static void* addr[kSlots] = {};
+  static int next = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int k = 0; k < kSlots; ++k)
+    if (keys[k] == ctx) {
+      *out = addr[k];
+      return RBF_OK;
+    }
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr)
+    return set_detail(RBF_ERR_CUDA, "cudaGetSymbolAddress(scratch)", e);
+  // A context handle can be reused after its context is destroyed; the slot is then looked up
+  // again above and overwritten here (round robin), never read stale for a live context other
+  // than the one that created it.
+  keys[next] = ctx;
+  addr[next] = p;
+  next = (next + 1) % kSlots;
+  *out = p;
   return RBF_OK;
 }
 
@@ -519,9 +560,20 @@ extern "C" int rbf_sm100_forward_noalloc(const float* X, const float* Y, float* 
   void* ws = nullptr;
   if ((st = noalloc_scratch(&ws))) return st;
   // The split pass rewrites every scratch byte the forward reads (norms, hi/lo splits) and
-  // resets the status word, so nothing left by an earlier call leaks into this one.
+  // resets the status word, so nothing left by an earlier call leaks into this one.  The status
+  // word stays readable through rbf_sm100_forward_noalloc_read_status until the next call.
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if ((st = cuda_status(launch_prep(X, Y, N, M, D, ws, s), "split pass launch"))) return st;
   return cuda_status(launch_forward_tc(X, Y, K, N, M, D, gamma, ws, wait_config_from_env(), s),
                      "forward launch");
+}
+
+extern "C" int rbf_sm100_forward_noalloc_read_status(rbf_stream_t stream, int* device_status) {
+  using namespace rbf;
+  if (device_status == nullptr) return set_detail(RBF_ERR_INVALID_ARGUMENT, "NULL output");
+  int st = check_device();
+  if (st) return st;
+  void* ws = nullptr;
+  if ((st = noalloc_scratch(&ws))) return st;
+  return rbf_sm100_read_status(ws, stream, device_status);
 }

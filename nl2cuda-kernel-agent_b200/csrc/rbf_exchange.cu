@@ -15,6 +15,9 @@
 //   3. barrier B (epoch 2*ctr + 2), released by the last block to finish step 2;
 //   4. gather: every row of dY from its owner's slot;
 //   5. the last block to finish advances ctr.
+// A barrier that runs out (a peer that never arrives) is sticky: the block sets tickets[2], the
+// counter is not advanced, and every later exchange on these buffers skips its work and
+// reports RBF_ERR_TIMEOUT until the caller rebuilds the buffers (zeroed flags and counters).
 // Two slots suffice: slot s is next zeroed (and added into, by its own rank only) two steps
 // later, after every rank has passed barrier A of the step in between, which each rank enters
 // only after its gather of this step.  No host synchronisation, and a captured CUDA graph of the
@@ -114,8 +117,14 @@ __global__ void __launch_bounds__(kThreads) rbf_dy_exchange_kernel(const Exchang
   ptx::griddep_wait();  // this rank's backward (its partial) is complete
   XT(1);
   __shared__ int s_ctr, s_ok;
-  if (threadIdx.x == 0) s_ctr = *reinterpret_cast<volatile int*>(a.ctr);
+  if (threadIdx.x == 0) {
+    s_ctr = *reinterpret_cast<volatile int*>(a.ctr);
+    // An earlier exchange on these buffers timed out: the ranks' epochs no longer agree.
+    s_ok = reinterpret_cast<volatile unsigned*>(a.tickets)[2] == 0u;
+    if (!s_ok) atomicExch(a.status, RBF_ERR_TIMEOUT);
+  }
   __syncthreads();
+  const bool usable = s_ok != 0;
   const int ctr = s_ctr;
   const int world = a.route.world, rank = a.route.rank;
   const int64_t slot = (int64_t)(ctr % kDySlots) * a.M * a.D;
@@ -124,10 +133,11 @@ __global__ void __launch_bounds__(kThreads) rbf_dy_exchange_kernel(const Exchang
   const bool two_phase = world > a.one_phase_max;
 
   // 1. Barrier A: every rank's partial is complete.
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && usable) {
     if (blockIdx.x == 0) signal_all(a, 2 * ctr + 1);
     XT(2);
     s_ok = wait_all(a, 2 * ctr + 1);
+    if (!s_ok) atomicExch(&a.tickets[2], 1u);
     XT(3);
   }
   __syncthreads();
@@ -170,6 +180,7 @@ __global__ void __launch_bounds__(kThreads) rbf_dy_exchange_kernel(const Exchang
           signal_all(a, 2 * ctr + 2);
         }
         s_ok = wait_all(a, 2 * ctr + 2);
+        if (!s_ok) atomicExch(&a.tickets[2], 1u);
         XT(5);
       }
     }
@@ -190,13 +201,15 @@ __global__ void __launch_bounds__(kThreads) rbf_dy_exchange_kernel(const Exchang
   __syncthreads();
   XT(6);
 
-  // 5. Advance the step counter once every block has read it and finished.
+  // 5. Advance the step counter once every block has read it and finished, unless a barrier
+  //    ran out (then the counter stays, and the sticky flag stops later exchanges).
   if (threadIdx.x == 0) {
+    __threadfence();  // this block's sticky-flag write before its ticket
     const unsigned t = atomicAdd(&a.tickets[1], 1u);
     if (t == gridDim.x - 1) {
       a.tickets[1] = 0u;
       __threadfence();
-      *a.ctr = ctr + 1;
+      if (reinterpret_cast<volatile unsigned*>(a.tickets)[2] == 0u) *a.ctr = ctr + 1;
     }
   }
 }

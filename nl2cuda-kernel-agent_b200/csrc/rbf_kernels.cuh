@@ -119,7 +119,7 @@ struct ExchangeArgs {
   DyRoute route;
   int* flags[kMaxRanks];
   int* ctr;
-  unsigned* tickets;  // two zeroed counters, reused across steps
+  unsigned* tickets;  // two zeroed counters reused across steps, then the sticky failure flag
   int one_phase_max;  // up to this many ranks: one barrier, every rank sums all partials
   int* status;
   unsigned long long timeout_ns;

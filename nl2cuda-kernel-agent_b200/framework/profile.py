@@ -147,18 +147,31 @@ def format_raw(recs):
     return "\n".join(lines)
 
 
-def ncu_commands(case, impl, py="python"):
-    """The two capture commands for one GPU (the plain run must exit 0 first)."""
+# The kernels worth a full capture, per case: one `ncu` command each, filtered to that kernel.
+CAPTURE_KERNELS = {
+    "rbf": ("rbf_fwd_tc_kernel", "rbf_bwd_tc_kernel"),
+    "cosine_sim": ("rbf_fwd_tc_kernel", "rbf_bwd_tc_kernel"),
+}
+
+
+def ncu_commands(case, impl, py="python", kernels=None):
+    """The capture commands for one GPU: the plain run (which must exit 0 first), the launch
+    list, and one section capture per kernel (`-k regex:<kernel>`, three launches at most) on the
+    case's own small size (a few GB on the device at most)."""
     run = f"{py} -m framework.profile --case {case}" + (f" --impl {impl}" if impl else "")
-    return [
+    cmds = [
         f"{run} && ncu --metrics gpu__time_duration.sum --clock-control none --csv "
         f"--log-file launches.csv {run}",
-        f"{run} && ncu --section SpeedOfLight --section MemoryWorkloadAnalysis "
-        f"--section WarpStateStats --metrics dram__bytes_read.sum,dram__bytes_write.sum,"
-        f"sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_elapsed "
-        f"--clock-control none -c 4 -o prof {run}",
-        "ncu -i prof.ncu-rep --page raw --csv > raw.csv",
     ]
+    for k in (kernels or CAPTURE_KERNELS.get(case, ("rbf_bwd_tc_kernel",))):
+        cmds.append(
+            f"{run} && ncu -k regex:{k} -c 3 --section SpeedOfLight "
+            f"--section MemoryWorkloadAnalysis --section WarpStateStats "
+            f"--metrics dram__bytes_read.sum,dram__bytes_write.sum,"
+            f"sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_elapsed "
+            f"--clock-control none -o prof_{k} {run}")
+        cmds.append(f"ncu -i prof_{k}.ncu-rep --page raw --csv > raw_{k}.csv")
+    return cmds
 
 
 # ----------------------------------------------------------------------------- torch.profiler

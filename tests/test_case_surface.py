@@ -26,22 +26,20 @@ def test_case_fields_match_reference_defaults():
 
 
 @pytest.mark.parametrize("seed,size", [(0, 128), (1, 64), (4, 64)])
-def test_make_inputs_reproduces_reference_stream(seed, size):
+def test_make_inputs_reproduces_reference_stream(seed, size, tmp_path):
     # Run in a child process so RBF_SIZE is read at import, as the reference's config does.
     code = (
         "import sys, numpy as np, torch; sys.path.insert(0, %r);"
         "from cases.rbf.reference import make_inputs;"
         "d = make_inputs(%d, torch.float32, 'cpu');"
         "np.savez(sys.argv[1], X=d['X'].numpy(), Y=d['Y'].numpy())" % (PKG, seed))
-    out = os.path.join(ROOT, "_work", f"mi_{seed}_{size}.npz")
-    os.makedirs(os.path.dirname(out), exist_ok=True)
+    out = str(tmp_path / f"mi_{seed}_{size}.npz")
     env = dict(os.environ, RBF_SIZE=str(size))
     subprocess.run([sys.executable, "-c", code, out], check=True, env=env)
     got = np.load(out)
     z = load(f"ref_makeinputs_seed{seed}_n{size}")
     np.testing.assert_array_equal(got["X"], z["X"])
     np.testing.assert_array_equal(got["Y"], z["Y"])
-    os.remove(out)
 
 
 @pytest.mark.parametrize("name", ["ref_makeinputs_seed0_n128", "ragged_n37_m50_d5",

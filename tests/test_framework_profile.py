@@ -40,6 +40,13 @@ def test_ncu_commands_keep_clock_control_none():
     assert any("--page raw --csv" in c for c in cmds)
 
 
+def test_ncu_section_captures_name_one_kernel_each():
+    cmds = [c for c in profile.ncu_commands("rbf", None) if "--section" in c]
+    assert len(cmds) == 2
+    for c, k in zip(cmds, ("rbf_fwd_tc_kernel", "rbf_bwd_tc_kernel")):
+        assert f"-k regex:{k}" in c and " -c 3 " in c
+
+
 def test_cli_summaries(capsys):
     assert profile.main(["--launches", os.path.join(FIX, "ncu_launches_sample.csv")]) == 0
     assert "kern_b" in capsys.readouterr().out

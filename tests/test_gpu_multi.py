@@ -1,7 +1,8 @@
 """Row-sharded forward + backward on 2 GPUs (skipped with fewer): the dY reduction fused into the
 backward over peer memory (shard.RoutedDy) against the NCCL all-reduce path and the oracle,
 CUDA-graph replays of the routed step, and the bounded cross-GPU wait running out when one rank
-never joins (no GPU fault: the waiting kernel returns RBF_ERR_TIMEOUT)."""
+never joins (no GPU fault: the waiting kernel returns RBF_ERR_TIMEOUT, the failure is sticky on
+those buffers, and the status-checking step raises)."""
 import os
 import socket
 
@@ -80,6 +81,14 @@ def _worker(rank, world, port, out_dir, one_phase_max):
             torch.cuda.synchronize(dev)
             assert native.read_status(ws) == 7
             os.environ.pop("RBF_WAIT_TIMEOUT_MS")
+            # The timeout is sticky: the counter did not advance, and the next exchange on the
+            # same buffers skips its work and reports the timeout at once.
+            assert route2.failed()
+            assert int(route2.counters[0].item()) == 0
+            native.dy_exchange(route2, ws)
+            assert native.read_status(ws) == 7
+            with pytest.raises(RuntimeError, match="timed out"):
+                shard.forward_backward_shard(Xd, Yd, Gd, GAMMA, route=route2, check_status=True)
             # the context is still usable
             assert torch.isfinite(native.rbf_forward(Xd, Yd, GAMMA)).all()
         torch.cuda.synchronize(dev)

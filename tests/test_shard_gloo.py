@@ -80,3 +80,51 @@ def test_two_rank_shard_matches_unsharded(tmp_path, world):
         np.testing.assert_allclose(z["K"], K[a:b], rtol=1e-6, atol=1e-7)
         np.testing.assert_allclose(z["dX"], dX[a:b], rtol=1e-5, atol=1e-6)
         np.testing.assert_allclose(z["dY"], dY, rtol=1e-5, atol=1e-6)
+
+
+class TimedOutCompute(OracleCompute):
+    """The native compute's status hook, faked: rank 1's device wait ran out (status 7)."""
+
+    def __init__(self, rank):
+        self.rank = rank
+
+    def status(self, state):
+        return 7 if self.rank == 1 else 0
+
+
+def _status_worker(rank, world, port, out_dir):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for p in (os.path.join(root, "nl2cuda-kernel-agent_b200"), root):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    X, Y, G = torch.randn(6, 3), torch.randn(5, 3), torch.randn(6, 5)
+    Xl, Gl = shard.shard_inputs(X, G, world, rank)
+    outcome = "ok"
+    try:
+        # The status is read before the dY collective: the failing rank raises and never joins
+        # it, so the check must not be left to a collective that would wait for it.
+        shard.forward_backward_shard(Xl, Y, Gl, 0.1, compute=TimedOutCompute(rank),
+                                     reduce_dy=False, check_status=True)
+    except RuntimeError as e:
+        outcome = "raised: " + str(e)
+    with open(os.path.join(out_dir, f"status{rank}.txt"), "w") as f:
+        f.write(outcome)
+    dist.destroy_process_group()
+
+
+def test_status_check_raises_on_the_rank_whose_wait_timed_out(tmp_path):
+    port = 30500 + (os.getpid() % 1000)
+    mp.spawn(_status_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    assert (tmp_path / "status0.txt").read_text() == "ok"
+    r1 = (tmp_path / "status1.txt").read_text()
+    assert r1.startswith("raised:") and "timed out" in r1
+
+
+def test_status_check_is_opt_in(monkeypatch):
+    monkeypatch.delenv("RBF_CHECK_STATUS", raising=False)
+    assert shard.check_status_default() is False
+    monkeypatch.setenv("RBF_CHECK_STATUS", "1")
+    assert shard.check_status_default() is True

@@ -2,18 +2,22 @@
 
 It exists for callers that cannot allocate device memory (an application whose allocator owns
 the device heap, a runtime that forbids cudaMalloc on its hot path, a plugin interface with no
-workspace argument): its workspace is a fixed array inside the library.  The test checks its K
-against rbf_sm100_forward's on two calls in a row (different inputs, so a stale workspace from
-the first call would show), and that an over-capacity size is refused with RBF_ERR_TOO_LARGE.
+workspace argument): its workspace is a fixed array inside the library.  The tests check its K
+against rbf_sm100_forward's and against the CPU oracle on two calls in a row (different inputs,
+so a stale workspace from the first call would show), that the calls allocate no device memory,
+that an over-capacity size is refused with RBF_ERR_TOO_LARGE, and that a device-side wait that
+runs out is reported through rbf_sm100_forward_noalloc_read_status.
 This file sorts last so that a run stopping at its first failure has run every other test.
 """
 import ctypes
+import os
 
 import numpy as np
 import pytest
 import torch
 
 from gpu_util import TOL, assert_gate, to_dev
+from oracle import oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -43,6 +47,56 @@ def test_noalloc_forward_matches_workspace_forward_twice(cuda_device):
         torch.cuda.synchronize()
         ref = native.rbf_forward(X, Y, gamma)
         assert_gate(f"call {call} K", K.cpu().numpy(), ref.cpu().numpy(), TOL)
+        rows = np.unique(r.integers(0, N, 16))
+        assert_gate(f"call {call} K vs oracle", K.cpu().numpy()[rows],
+                    oracle.forward_rows(X.cpu().numpy(), Y.cpu().numpy(), gamma, rows), TOL)
+
+
+def test_noalloc_forward_allocates_no_device_memory(cuda_device):
+    from cases.rbf import native
+    L = native.lib()
+    N = M = 4096  # the largest c1-sized call: (N + M) * 129 * 4 B, within the 16 MiB array
+    gen = torch.Generator(device=cuda_device).manual_seed(5)
+    X = torch.randn(N, 64, device=cuda_device, generator=gen)
+    Y = torch.randn(M, 64, device=cuda_device, generator=gen)
+    K = torch.empty(N, M, device=cuda_device)
+    assert _noalloc(L, X, Y, K, 1 / 64) == 0  # warm-up: symbol lookup, module load
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    alloc0 = torch.cuda.memory_allocated()
+    for _ in range(5):
+        assert _noalloc(L, X, Y, K, 1 / 64) == 0
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    assert torch.cuda.memory_allocated() == alloc0
+
+
+def test_noalloc_wait_timeout_is_reported(cuda_device):
+    from cases.rbf import native
+    L = native.lib()
+    rs = L.rbf_sm100_forward_noalloc_read_status
+    rs.restype = ctypes.c_int
+    rs.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]
+    r = np.random.default_rng(3)
+    X, Y = to_dev(r.standard_normal((256, 64)), r.standard_normal((300, 64)))
+    K = torch.zeros(256, 300, device=cuda_device)
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    os.environ["RBF_DEBUG_SKIP_FIRST_LOAD"] = "1"
+    os.environ["RBF_WAIT_TIMEOUT_MS"] = "100"
+    try:
+        assert _noalloc(L, X, Y, K, 1 / 64) == 0
+        out = ctypes.c_int(-1)
+        assert rs(s, ctypes.byref(out)) == 0
+    finally:
+        del os.environ["RBF_DEBUG_SKIP_FIRST_LOAD"]
+        del os.environ["RBF_WAIT_TIMEOUT_MS"]
+    assert out.value == 7  # RBF_ERR_TIMEOUT
+    # A normal call right after is correct and reports OK.
+    assert _noalloc(L, X, Y, K, 1 / 64) == 0
+    out = ctypes.c_int(-1)
+    assert rs(s, ctypes.byref(out)) == 0 and out.value == 0
+    assert_gate("K after timeout", K.cpu().numpy(),
+                oracle.forward(X.cpu().numpy(), Y.cpu().numpy(), 1 / 64), TOL)
 
 
 def test_noalloc_rejects_sizes_beyond_capacity(cuda_device):
