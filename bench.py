@@ -453,6 +453,10 @@ def main():
     reps = max(args.steps, 5)
     ms_fwd = time_alone(fwd_graph, reps)
     ms_bwd = time_alone(bwd_graph, reps)
+    # The one-call forward + backward (rbf_sm100_forward_backward): this rank's step without
+    # the dY reduction.
+    fused_graph, _ = capture(lambda: native.rbf_forward_backward(X, Y, G, g))
+    ms_fused = time_alone(fused_graph, reps)
     pk = peaks()
     fwd_bytes = 4 * n * M + 4 * (n + M) * D
     bwd_bytes = 8 * n * M + 8 * (n + M) * D
@@ -515,6 +519,7 @@ def main():
                            if dy_reduce == "peer" else ", dY all-reduce (NCCL)"
                            if world > 1 else "")},
             "ms_fwd": round(ms_fwd, 5), "ms_bwd": round(ms_bwd, 5),
+            "ms_fused": round(ms_fused, 5),
             "pct_roofline_step": round(100.0 * t_roof / (ms * 1e-3), 2),
             "roofline_step_us": round(t_roof * 1e6, 2),
             "roofline": roofline,

@@ -85,6 +85,13 @@ RBF_API int rbf_sm100_forward(const float* X, const float* Y, float* K,
  * twice.  K is the forward's output (the reference's autograd saves it, cases/rbf/op.py:31-32).
  * dX and dY are fully overwritten.
  * ------------------------------------------------------------------------------------------- */
+/* RBF_DETERMINISTIC=1 in the environment (read at every call) makes the backward entries
+ * bit-reproducible run to run: each tile's dX / dY contribution goes to its own slot in the
+ * workspace and a finalize pass sums the slots in a fixed order, instead of atomic adds.  The
+ * workspace then needs about 4 * (ceil(M/128) * N' + ceil(N/128) * M) * (D + 1) more bytes
+ * (N' = N rounded up to 128); rbf_sm100_backward_workspace_bytes includes them while the
+ * variable is set, so size the workspace after setting it.  A smaller workspace is refused
+ * (RBF_ERR_WORKSPACE).  M % 4 != 0 runs CUDA-core kernels that are deterministic already. */
 RBF_API size_t rbf_sm100_backward_workspace_bytes(int64_t N, int64_t M, int64_t D);
 
 RBF_API int rbf_sm100_backward(const float* X, const float* Y, const float* G, const float* K,
@@ -101,6 +108,21 @@ RBF_API int rbf_sm100_backward_prepared(const float* X, const float* Y, const fl
                                 float* dX, float* dY,
                                 int64_t N, int64_t M, int64_t D, float gamma,
                                 void* workspace, size_t workspace_bytes, rbf_stream_t stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Forward and backward in one call, for callers that hold the upstream gradient G before the
+ * forward runs (a fixed loss, a training harness).  Replaces the pair of calls the reference's
+ * autograd op makes, RBFFunction.forward then RBFFunction.backward (reference
+ * cases/rbf/op.py:27-37): K = exp(-gamma ||x_i - y_j||^2) is written to K and [dX, dY] of
+ * sum(G * K) to dX and dY.  The X/Y split is made once and shared by both passes, and the
+ * backward kernels follow the forward on `stream` by programmatic dependent launch.  The
+ * workspace is the backward's, rbf_sm100_backward_workspace_bytes(N, M, D).  Results are those
+ * of rbf_sm100_forward followed by rbf_sm100_backward_prepared.
+ * ------------------------------------------------------------------------------------------- */
+RBF_API int rbf_sm100_forward_backward(const float* X, const float* Y, const float* G, float* K,
+                               float* dX, float* dY,
+                               int64_t N, int64_t M, int64_t D, float gamma,
+                               void* workspace, size_t workspace_bytes, rbf_stream_t stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Multi-GPU row sharding helper.  The caller owns rows [row0, row0+N_local) of X, G and K; Y is

@@ -44,7 +44,7 @@ def lib():
             L.rbf_sm100_forward.argtypes = [_F, _F, _F, _I64, _I64, _I64, ctypes.c_float, _F,
                                             _SZ, _F]
             for fn in ("rbf_sm100_backward", "rbf_sm100_backward_prepared",
-                       "rbf_sm100_backward_shard"):
+                       "rbf_sm100_backward_shard", "rbf_sm100_forward_backward"):
                 getattr(L, fn).restype = ctypes.c_int
                 getattr(L, fn).argtypes = [_F, _F, _F, _F, _F, _F, _I64, _I64, _I64,
                                            ctypes.c_float, _F, _SZ, _F]
@@ -149,6 +149,28 @@ def rbf_backward(X, Y, G, K, gamma, workspace=None, entry="rbf_sm100_backward"):
         check(fn(_ptr(X), _ptr(Y), _ptr(G), _ptr(K), _ptr(dX), _ptr(dY), N, M, D, float(gamma),
                  _ptr(ws), ws.numel(), _stream(X.device)), fn.__name__)
     return [dX, dY]
+
+
+def rbf_forward_backward(X, Y, G, gamma):
+    """[K, dX, dY] in one call (``rbf_sm100_forward_backward``): the forward of X, Y and the
+    backward of sum(G * K), for a G known before the forward; the same values as
+    ``forward_with_workspace`` followed by ``rbf_backward`` with that workspace."""
+    _check_2d(("X", "Y", "G"), (X, Y, G))
+    X, Y, G = _operand(X), _operand(Y), _operand(G)
+    N, D = X.shape
+    M = Y.size(0)
+    if Y.size(1) != D or tuple(G.shape) != (N, M):
+        raise RuntimeError("shape mismatch: need X [N,D], Y [M,D], G [N,M]")
+    with torch.cuda.device(X.device):
+        K = torch.empty((N, M), dtype=torch.float32, device=X.device)
+        dX = torch.empty_like(X)
+        dY = torch.empty_like(Y)
+        ws = new_workspace(N, M, D, X.device)
+        check(lib().rbf_sm100_forward_backward(_ptr(X), _ptr(Y), _ptr(G), _ptr(K), _ptr(dX),
+                                               _ptr(dY), N, M, D, float(gamma), _ptr(ws),
+                                               ws.numel(), _stream(X.device)),
+              "rbf_sm100_forward_backward")
+    return [K, dX, dY]
 
 
 # The ctypes helpers above, shared with the other case bound to this library (cosine_sim).

@@ -25,11 +25,17 @@ bool pdl_enabled() {
   return on;
 }
 
+bool deterministic_backward() {
+  const char* s = std::getenv("RBF_DETERMINISTIC");
+  return s != nullptr && std::atoi(s) != 0;
+}
+
 WaitConfig wait_config_from_env() {
   WaitConfig w;
   w.timeout_ns = 2000ull * 1000000ull;
   w.debug_skip_first_load = 0;
   w.fwd_pair = 0;
+  w.deterministic = deterministic_backward() ? 1 : 0;
   if (const char* s = std::getenv("RBF_FWD_PAIR")) w.fwd_pair = std::atoi(s) != 0;
   if (const char* s = std::getenv("RBF_WAIT_TIMEOUT_MS")) {
     const long long ms = std::atoll(s);
@@ -275,6 +281,22 @@ int rbf_sm100_backward_prepared(const float* X, const float* Y, const float* G, 
                                 rbf_stream_t stream) {
   return backward_impl(X, Y, G, K, dX, dY, N, M, D, gamma, workspace, workspace_bytes,
                        reinterpret_cast<cudaStream_t>(stream), true);
+}
+
+int rbf_sm100_forward_backward(const float* X, const float* Y, const float* G, float* K,
+                               float* dX, float* dY, int64_t N, int64_t M, int64_t D, float gamma,
+                               void* workspace, size_t workspace_bytes, rbf_stream_t stream) {
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // Every backward operand is checked before the forward runs, so a refused call writes nothing.
+  int st = check_shape(N, M, D, gamma);
+  if (st) return st;
+  if ((st = check_ptr(G, N * M, "G"))) return st;
+  if ((st = check_ptr(dX, N * D, "dX"))) return st;
+  if ((st = check_ptr(dY, M * D, "dY"))) return st;
+  if (workspace_bytes < rbf_sm100_backward_workspace_bytes(N, M, D))
+    return set_detail(RBF_ERR_WORKSPACE, "forward-backward needs the backward workspace");
+  if ((st = forward_impl(X, Y, K, N, M, D, gamma, workspace, workspace_bytes, s))) return st;
+  return backward_impl(X, Y, G, K, dX, dY, N, M, D, gamma, workspace, workspace_bytes, s, true);
 }
 
 int rbf_sm100_backward_shard(const float* X_local, const float* Y, const float* G_local,

@@ -104,6 +104,12 @@ struct BwdArgs {
   int64_t static_rows;   // group rows [0, static_rows) are split into contiguous per-CTA ranges;
   int* counter;          // tiles from static_rows * group on are claimed from this counter
   DyRoute route;  // world > 0: dY partials go to this rank's slot of the routed buffers
+  int det;        // deterministic mode: every tile stores its partials into its own slot
+  float* dxp;     // [tiles_j][Npad][D]   -c * (W Y) partial of tile (ib, jb), rows ib*128..
+  float* rsp;     // [tiles_j][Npad]      rowsum partial of tile (ib, jb)
+  float* dyp;     // [tiles_i][M][D]      -c * (W^T X) partial of tile (ib, jb), rows jb*128..
+  float* csp;     // [tiles_i][M]         colsum partial of tile (ib, jb)
+  int64_t Npad;   // N rounded up to the tile edge
   int ablate;     // development builds only (RBF_TRACE): 1 skip dX reduce, 2 skip rowsum add,
                   // 4 C-warps skip W^T, 8 R-warps skip W, 16 no MMAs, 32 skip dY flush
 };
@@ -155,8 +161,10 @@ __device__ __forceinline__ TileCoord tile_of(int64_t u, const BwdArgs& a) {
   return c;
 }
 
-__device__ __forceinline__ bool same_segment(const TileCoord& p, const TileCoord& q) {
-  return p.slice == q.slice && p.jb == q.jb;
+// Consecutive tiles of one dY segment share the dY accumulator.  Deterministic mode: every
+// tile is a segment of its own (its dY partial goes to its own slot).
+__device__ __forceinline__ bool same_segment(const TileCoord& p, const TileCoord& q, bool det) {
+  return !det && p.slice == q.slice && p.jb == q.jb;
 }
 
 // The CTA's tile sequence (its static range, then tiles claimed from the global counter) is
@@ -238,6 +246,25 @@ __device__ __forceinline__ void flush_row(float* out, const float* src, int64_t 
   }
 }
 
+// Deterministic mode: out[r, d0 + e] = scale * acc[e] for e < DS, d0 + e < D (plain stores).
+template <int DS>
+__device__ __forceinline__ void store_row(float* out, int64_t r, int64_t D, int d0, float scale,
+                                          const uint32_t* acc) {
+  float* o = out + r * D + d0;
+  const int n = (D - d0) < DS ? (int)(D - d0) : DS;
+  if (n == DS && (D & 3) == 0) {
+#pragma unroll
+    for (int e = 0; e < DS; e += 4)
+      *reinterpret_cast<float4*>(o + e) =
+          make_float4(scale * __uint_as_float(acc[e]), scale * __uint_as_float(acc[e + 1]),
+                      scale * __uint_as_float(acc[e + 2]), scale * __uint_as_float(acc[e + 3]));
+  } else {
+#pragma unroll
+    for (int e = 0; e < DS; ++e)
+      if (e < n) o[e] = scale * __uint_as_float(acc[e]);
+  }
+}
+
 // Load DS accumulator columns of this thread's TMEM lane.
 template <int DS>
 __device__ __forceinline__ void tmem_load_row(uint32_t taddr, uint32_t (&v)[64]) {
@@ -263,7 +290,7 @@ __device__ __forceinline__ void tmem_st_n(uint32_t taddr, const uint32_t* r) {
 #endif
 constexpr int CB = RBF_CB;  // rows of W^T a C-warp converts per TMEM store (code size vs. batching)
 
-template <int DS, bool DOT = false>
+template <int DS, bool DOT = false, bool DET = false>
 __global__ void __launch_bounds__(THREADS, 1)
     rbf_bwd_tc_kernel(const __grid_constant__ CUtensorMap tm_g,
                       const __grid_constant__ CUtensorMap tm_k,
@@ -417,7 +444,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!strips_done && ss == 4 && n_ys + 4 >= n_strips) {
           const TileCoord tc = tile_of(t, a);
           nxt = fetch();
-          if (!publish(t, nxt < 0 || !same_segment(tile_of(nxt, a), tc))) { ok = false; break; }
+          if (!publish(t, nxt < 0 || !same_segment(tile_of(nxt, a), tc, DET))) { ok = false; break; }
           if ((n_strips >> 2) & 1u) slot1 = tc; else slot0 = tc;
           i0 = tc.ib * BT;
           j0 = tc.jb * BT;
@@ -545,7 +572,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!sched_pop(sq, false, a, t, seg_end)) { ok = false; break; }
         if (t < 0) break;
         const TileCoord tc = tile_of(t, a);
-        if (!same_segment(tc, cur)) {
+        if (!same_segment(tc, cur, DET)) {
           cur = tc;
           // The C-warps drained the dY accumulator of the previous segment.
           if (!ptx::mbar_wait_bounded(dy_empty, dye_ph ^ 1, a.status, a.timeout_ns)) { ok = false; break; }
@@ -660,7 +687,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!sched_pop(sq, true, a, t, seg_end)) { ok = false; break; }
       if (t < 0) break;
       const TileCoord tc = tile_of(t, a);
-      if (!same_segment(tc, cur)) {
+      if (!same_segment(tc, cur, DET)) {
         cur = tc;
         colsum = 0.f;
       }
@@ -724,8 +751,16 @@ __global__ void __launch_bounds__(THREADS, 1)
 #ifdef RBF_TRACE
         if (a.ablate & 32) continue;
 #endif
-        float* dst = a.route.world > 0 ? route_dst : a.dY;
-        if (j < a.M) flush_row<DS, !DOT>(dst, a.Y, j, a.D, tc.slice * DS, a.c, colsum, accv);
+        if constexpr (DET) {
+          if (j < a.M) {
+            const int64_t slot = (int64_t)tc.ib * a.M + j;
+            store_row<DS>(a.dyp, slot, a.D, tc.slice * DS, -a.c, accv);
+            if (!DOT && tc.slice == 0) a.csp[slot] = colsum;
+          }
+        } else {
+          float* dst = a.route.world > 0 ? route_dst : a.dY;
+          if (j < a.M) flush_row<DS, !DOT>(dst, a.Y, j, a.D, tc.slice * DS, a.c, colsum, accv);
+        }
         if (lane == 0 && q == 0) TRACE(4, 50);
       }
     }
@@ -741,7 +776,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     bool ok = true, pending = false;
     float prev_rowsum = 0.f;
     int64_t prev_i = 0;
-    int prev_d0 = 0;
+    int prev_d0 = 0, prev_jb = 0;
     auto flush_prev = [&]() -> bool {
       if (!ptx::mbar_wait_bounded(dx_full, dxf_ph, a.status, a.timeout_ns)) return false;
       dxf_ph ^= 1;
@@ -751,13 +786,22 @@ __global__ void __launch_bounds__(THREADS, 1)
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(dx_empty);
-      if (!a.tma_flush) {
+      // Deterministic mode: this tile's partial goes to row slot_row of its j-block's slot.
+      const int64_t slot_row = DET ? (int64_t)prev_jb * a.Npad + prev_i : 0;
+      if constexpr (DET) {
+        if (!DOT && prev_i < a.N && prev_d0 == 0) a.rsp[slot_row] = prev_rowsum;
+        if (!a.tma_flush) {
+          if (prev_i < a.N) store_row<DS>(a.dxp, slot_row, a.D, prev_d0, -a.c, accv);
+          return true;
+        }
+      }
+      if (!DET && !a.tma_flush) {
         if (prev_i < a.N) flush_row<DS, !DOT>(a.dX, a.X, prev_i, a.D, prev_d0, a.c, prev_rowsum, accv);
         return true;
       }
       // -c * acc goes through shared memory to a TMA reduce-add (32 rows x DS, coalesced in L2);
       // c * rowsum * x is added once per row by the finalize pass from the rowsum vector.
-      if (!DOT && prev_i < a.N && prev_d0 == 0 && !(a.ablate & 2))
+      if (!DET && !DOT && prev_i < a.N && prev_d0 == 0 && !(a.ablate & 2))
         red_add1(a.rowsum + prev_i, prev_rowsum);
       uint8_t* stg = staging + q * C::STAGING;
       if (lane == 0) ptx::bulk_wait_read<0>();  // the previous reduce has read the buffer
@@ -777,8 +821,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0 && !(a.ablate & 1)) {
 #pragma unroll
-        for (int bx = 0; bx < DS / 32; ++bx)
-          ptx::tma_reduce_add_2d(&tm_dx, stg + bx * BOX, prev_d0 + 32 * bx, (int)prev_i);
+        for (int bx = 0; bx < DS / 32; ++bx) {
+          if constexpr (DET)
+            ptx::tma_store_2d(&tm_dx, stg + bx * BOX, prev_d0 + 32 * bx, (int)slot_row);
+          else
+            ptx::tma_reduce_add_2d(&tm_dx, stg + bx * BOX, prev_d0 + 32 * bx, (int)prev_i);
+        }
         ptx::bulk_commit();
       }
       return true;
@@ -850,6 +898,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       prev_rowsum = rowsum;
       prev_i = (int64_t)tc.ib * BT + q * 32 + lane;
       prev_d0 = tc.slice * DS;
+      prev_jb = tc.jb;
     }
     if (ok && pending) flush_prev();
     if (lane == 0) ptx::bulk_wait<0>();  // reduces complete before the CTA exits
@@ -911,13 +960,70 @@ __global__ void __launch_bounds__(256) rbf_bwd_zero_kernel(float* __restrict__ a
   }
 }
 
+// Deterministic mode: dX[i,:] = the tiles' -c * (W Y) partials summed over j-blocks in order,
+// + c * (their row sums, in order) * x_i; dY likewise over i-blocks.  One thread per output
+// element, so every sum has one fixed order.  sums = 0 (cosine case): the partials only.
+__global__ void __launch_bounds__(256) rbf_bwd_det_finalize_kernel(
+    const float* __restrict__ X, const float* __restrict__ Y, const float* __restrict__ dxp,
+    const float* __restrict__ rsp, const float* __restrict__ dyp, const float* __restrict__ csp,
+    float* __restrict__ dX, float* __restrict__ dY, int64_t N, int64_t M, int64_t D, int64_t Npad,
+    int tiles_j, int tiles_i, float c, int sums) {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < (N + M) * D; k += stride) {
+    if (k < N * D) {
+      const int64_t i = k / D, d = k - i * D;
+      float acc = 0.f, rs = 0.f;
+      for (int jb = 0; jb < tiles_j; ++jb) {
+        acc += dxp[((int64_t)jb * Npad + i) * D + d];
+        if (sums) rs += rsp[(int64_t)jb * Npad + i];
+      }
+      dX[k] = sums ? fmaf(c * rs, X[k], acc) : acc;
+    } else {
+      const int64_t k2 = k - N * D, j = k2 / D, d = k2 - j * D;
+      float acc = 0.f, cs = 0.f;
+      for (int ib = 0; ib < tiles_i; ++ib) {
+        acc += dyp[((int64_t)ib * M + j) * D + d];
+        if (sums) cs += csp[(int64_t)ib * M + j];
+      }
+      dY[k2] = sums ? fmaf(c * cs, Y[k2], acc) : acc;
+    }
+  }
+}
+
 }  // namespace
 
-// Scratch after the split-pass layout: the rowsum vector [N] and the tile counter.
+// Scratch after the split-pass layout: the rowsum vector [N] and the tile counter; in
+// deterministic mode, then the per-tile partial slots.
 static int64_t rowsum_bytes(int64_t N) { return round_up((int64_t)sizeof(float) * N, (int64_t)kAlign); }
 
+struct DetLayout {
+  size_t dxp, rsp, dyp, csp, end;  // byte offsets after the split-pass layout
+  int64_t Npad;
+};
+
+static DetLayout det_layout(int64_t N, int64_t M, int64_t D) {
+  DetLayout d;
+  const int64_t tj = ceil_div(M, BT), ti = ceil_div(N, BT);
+  d.Npad = round_up(N, (int64_t)BT);
+  size_t off = (size_t)(rowsum_bytes(N) + kAlign);
+  auto take = [&](int64_t bytes) {
+    const size_t o = off;
+    off = (size_t)round_up((int64_t)off + bytes, (int64_t)kAlign);
+    return o;
+  };
+  d.dxp = take(4 * tj * d.Npad * D);
+  d.rsp = take(4 * tj * d.Npad);
+  d.dyp = take(4 * ti * M * D);
+  d.csp = take(4 * ti * M);
+  d.end = off;
+  return d;
+}
+
 size_t backward_scratch_bytes(int64_t N, int64_t M, int64_t D) {
-  (void)M; (void)D;
+  if (deterministic_backward() && N > 0 && M > 0 && D > 0 && (M % 4) == 0)
+    return det_layout(N, M, D).end;
   return (size_t)(rowsum_bytes(N) + kAlign);
 }
 
@@ -938,7 +1044,17 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
   float* rowsum = ws_at<float>(ws, L.end);
   int* counter = ws_at<int>(ws, L.end + rowsum_bytes(N));
   const bool work = N > 0 && M > 0 && D > 0;
-  {
+  // Deterministic mode (not with a routed dY, whose partials already sit in per-rank slots):
+  // nothing is accumulated in place, so only the tile counter is zeroed.
+  const bool det = wc.deterministic && !routed && work;
+  const DetLayout DL = det ? det_layout(N, M, D) : DetLayout{};
+  if (det) {
+    if ((e = launch_kernel(rbf_bwd_zero_kernel, dim3(1), dim3(256), 0, stream, dX, (int64_t)0,
+                           dY, (int64_t)0, reinterpret_cast<float*>(counter), (int64_t)1,
+                           (const int*)nullptr)) != cudaSuccess)
+      return e;
+    note_launches(1);
+  } else {
     // rowsum and the counter are adjacent: one range covers both (or just the counter).
     float* zc = (work && tma_flush) ? rowsum : reinterpret_cast<float*>(counter);
     const int64_t nz = (work && tma_flush) ? rowsum_bytes(N) / 4 + 1 : (work ? 1 : 0);
@@ -971,7 +1087,11 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
       !make_tmap_2d(&tyl, ws_at<float>(ws, L.ylo), M, L.Dp, L.Dp, 32, 32, mn))
     return cudaErrorInvalidValue;
   if (tma_flush) {
-    if (!make_tmap_2d(&tdx, dX, N, D, D, 32, 32)) return cudaErrorInvalidValue;
+    // Deterministic mode: the dX tile partials are stored into their slots, [tiles_j * Npad] rows.
+    if (!(det ? make_tmap_2d(&tdx, ws_at<float>(ws, L.end + DL.dxp), ceil_div(M, BT) * DL.Npad, D,
+                             D, 32, 32)
+              : make_tmap_2d(&tdx, dX, N, D, D, 32, 32)))
+      return cudaErrorInvalidValue;
   } else {
     tdx = tg;  // unused
   }
@@ -992,6 +1112,12 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
   a.counter = counter;
   a.route = routed ? *route : DyRoute{};
   if (!routed) a.route.world = 0;
+  a.det = det ? 1 : 0;
+  a.Npad = DL.Npad;
+  a.dxp = det ? ws_at<float>(ws, L.end + DL.dxp) : nullptr;
+  a.rsp = det ? ws_at<float>(ws, L.end + DL.rsp) : nullptr;
+  a.dyp = det ? ws_at<float>(ws, L.end + DL.dyp) : nullptr;
+  a.csp = det ? ws_at<float>(ws, L.end + DL.csp) : nullptr;
   const int grid = (int)std::min<int64_t>(a.total_tiles, device_sm_count());
   {
     // Group width (RBF_BWD_GROUP, default 4) and the share of tiles handed out dynamically
@@ -1019,15 +1145,34 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
     return launch_kernel(kernel, dim3(grid), dim3(THREADS), smem, stream, tg, tk, txh, txl, tyh,
                          tyl, tdx, a);
   };
-  if (DS == 32)
+  if (det) {
+    if (DS == 32)
+      e = dot ? launch(rbf_bwd_tc_kernel<32, true, true>, Cfg<32>::SMEM)
+              : launch(rbf_bwd_tc_kernel<32, false, true>, Cfg<32>::SMEM);
+    else
+      e = dot ? launch(rbf_bwd_tc_kernel<64, true, true>, Cfg<64>::SMEM)
+              : launch(rbf_bwd_tc_kernel<64, false, true>, Cfg<64>::SMEM);
+  } else if (DS == 32) {
     e = dot ? launch(rbf_bwd_tc_kernel<32, true>, Cfg<32>::SMEM)
             : launch(rbf_bwd_tc_kernel<32, false>, Cfg<32>::SMEM);
-  else
+  } else {
     e = dot ? launch(rbf_bwd_tc_kernel<64, true>, Cfg<64>::SMEM)
             : launch(rbf_bwd_tc_kernel<64, false>, Cfg<64>::SMEM);
+  }
   if (e != cudaSuccess) return e;
   note_launches(1);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if (det) {
+    const int64_t total = (N + M) * D;
+    const int64_t blocks = std::min<int64_t>(ceil_div(total, 256), 8 * device_sm_count());
+    if ((e = launch_kernel(rbf_bwd_det_finalize_kernel, dim3((unsigned)blocks), dim3(256), 0,
+                           stream, X, Y, (const float*)a.dxp, (const float*)a.rsp,
+                           (const float*)a.dyp, (const float*)a.csp, dX, dY, N, M, D, DL.Npad,
+                           a.tiles_j, a.tiles_i, a.c, dot ? 0 : 1)) != cudaSuccess)
+      return e;
+    note_launches(1);
+    return cudaGetLastError();
+  }
   if (tma_flush && !dot) {
     const int64_t n4 = N * (D / 4);
     if ((e = launch_kernel(rbf_bwd_finalize_kernel, dim3((unsigned)ceil_div(n4, 256)), dim3(256), 0,

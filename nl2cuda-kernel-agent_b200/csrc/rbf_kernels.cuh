@@ -60,8 +60,12 @@ struct WaitConfig {
   unsigned long long timeout_ns;
   int debug_skip_first_load;
   int fwd_pair;  // RBF_FWD_PAIR (default 0): 1 runs the D <= 64 forward on two-CTA clusters
+  int deterministic;  // RBF_DETERMINISTIC (default 0): 1 makes the backward bit-reproducible
 };
 WaitConfig wait_config_from_env();
+// RBF_DETERMINISTIC set to a non-zero integer (read at every call): the backward stores each
+// tile's partials into its own workspace slot and sums the slots in a fixed order.
+bool deterministic_backward();
 
 // Row-sharded dY reduction without a library collective: every rank's backward accumulates its
 // dY partial into slot (*ctr % kDySlots) of its own buffer bufs[rank] (peer-visible memory, e.g.

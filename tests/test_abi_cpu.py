@@ -116,3 +116,21 @@ def test_cosine_host_side_validation(lib):
     assert bwd(A, A, A, 8, 8, 4, 1e-8, A, wsb - 1) == WORKSPACE
     assert bwd(0, A, A, 8, 8, 4, 1e-8, A, wsb) == INVALID
     assert bwd(A, A, A, 8, 8, 5000, 1e-8, A, 1 << 30) == UNSUPPORTED
+
+
+def test_deterministic_backward_workspace_holds_the_tile_slots(lib, monkeypatch):
+    """RBF_DETERMINISTIC=1 (read at every call) adds the per-tile partial slots of dX and dY,
+    4 * (tiles_j * Npad + tiles_i * M) * (D + 1) bytes, to the backward workspace."""
+    b = lib.rbf_sm100_backward_workspace_bytes
+    N, M, D = 300, 400, 64
+    monkeypatch.delenv("RBF_DETERMINISTIC", raising=False)
+    base = b(N, M, D)
+    monkeypatch.setenv("RBF_DETERMINISTIC", "1")
+    det = b(N, M, D)
+    tiles_j, tiles_i, npad = 4, 3, 384
+    assert det - base >= 4 * (tiles_j * npad + tiles_i * M) * (D + 1)
+    assert det - base <= 4 * (tiles_j * npad + tiles_i * M) * (D + 1) + 4 * 256
+    ragged = b(N, 401, D)  # M % 4 != 0: the CUDA-core kernels, deterministic already
+    monkeypatch.setenv("RBF_DETERMINISTIC", "0")
+    assert b(N, M, D) == base
+    assert b(N, 401, D) == ragged

@@ -155,3 +155,47 @@ def test_forward_pair_and_single_cta_variants(N, M, D, gamma, cuda_device, monke
         out[flag] = K.cpu().numpy()
         assert_gate(f"K pair={flag}", out[flag][rows], Kr)
     np.testing.assert_allclose(out["1"], out["0"], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("N,M,D,gamma", [(300, 200, 64, 0.02), (517, 1000, 37, 1 / 37),
+                                         (129, 260, 32, 0.5 / 32), (7, 129, 3, 0.3),
+                                         (1000, 333, 256, 1 / 256)])
+def test_forward_backward_entry(N, M, D, gamma, cuda_device):
+    """rbf_sm100_forward_backward: the two-call path's K, dX, dY, and the oracle's."""
+    from cases.rbf import native
+    r = np.random.default_rng(N + 7 * M + D)
+    X = r.standard_normal((N, D)).astype(np.float32)
+    Y = r.standard_normal((M, D)).astype(np.float32)
+    G = r.standard_normal((N, M)).astype(np.float32)
+    Xd, Yd, Gd = to_dev(X, Y, G)
+    K, dX, dY = native.rbf_forward_backward(Xd, Yd, Gd, gamma)
+    K2, ws = native.forward_with_workspace(Xd, Yd, gamma)
+    dX2, dY2 = native.rbf_backward(Xd, Yd, Gd, K2, gamma, workspace=ws)
+    assert torch.equal(K, K2)
+    # The backward's atomic flushes add in a run-dependent fp32 order.
+    torch.testing.assert_close(dX, dX2, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(dY, dY2, rtol=1e-4, atol=1e-4)
+    assert_gate("K", K.cpu().numpy(), oracle.forward(X, Y, gamma))
+    dXr, dYr = oracle.backward(X, Y, G, gamma)
+    assert_gate("dX", dX.cpu().numpy(), dXr)
+    assert_gate("dY", dY.cpu().numpy(), dYr)
+
+
+def test_forward_backward_entry_refuses_the_forward_workspace(cuda_device):
+    from cases.rbf import native
+    L = native.lib()
+    X = torch.randn(64, 64, device="cuda")
+    G = torch.randn(64, 64, device="cuda")
+    K = torch.full((64, 64), 7.0, device="cuda")
+    dX, dY = torch.empty(64, 64, device="cuda"), torch.empty(64, 64, device="cuda")
+    small = L.rbf_sm100_forward_workspace_bytes(64, 64, 64)
+    assert small < L.rbf_sm100_backward_workspace_bytes(64, 64, 64)
+    ws = torch.empty(small, dtype=torch.uint8, device="cuda")
+    vp = ctypes.c_void_p
+    st = L.rbf_sm100_forward_backward(vp(X.data_ptr()), vp(X.data_ptr()), vp(G.data_ptr()),
+                                      vp(K.data_ptr()), vp(dX.data_ptr()), vp(dY.data_ptr()),
+                                      64, 64, 64, 0.1, vp(ws.data_ptr()), small,
+                                      vp(torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert st == 3  # RBF_ERR_WORKSPACE
+    assert bool((K == 7.0).all())  # refused before the forward ran
