@@ -123,7 +123,9 @@ struct TileCoord {
 // (code << 56 | globaltimer).  Read back with rbf_debug_trace().
 __device__ unsigned long long g_trace[8][1024];
 __device__ int g_trace_n[8];
-__device__ unsigned long long g_cta_span[1024][2];
+// Per CTA: [0] start (after setup), [1] end | smid << 48, [2] released by the previous kernel,
+// [3] last strip issued | tiles << 48.
+__device__ unsigned long long g_cta_span[1024][4];
 __device__ __forceinline__ void trace(int role, int code) {
   if (blockIdx.x != 0) return;
   const int n = g_trace_n[role];
@@ -382,6 +384,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0 && blockIdx.x < 1024) g_cta_span[blockIdx.x][0] = ptx::globaltimer() & ((1ull << 48) - 1);
 #endif
   ptx::griddep_wait();  // outputs zeroed and the workspace written by the previous kernels
+#ifdef RBF_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < 1024) g_cta_span[blockIdx.x][2] = ptx::globaltimer() & ((1ull << 48) - 1);
+#endif
 
   SchedRing sq = {sq_tile, sq_seg_end, sq_full, sq_empty, 0, 0};
 
@@ -507,6 +512,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           __nanosleep(32);  // neither ring has room: leave the issue slots to the other warps
         }
       }
+#ifdef RBF_TRACE
+      if (blockIdx.x < 1024)
+        g_cta_span[blockIdx.x][3] = (ptx::globaltimer() & ((1ull << 48) - 1)) | ((unsigned long long)(n_strips / 4) << 48);
+#endif
       if (ok && !publish(-1, true)) ok = false;
       if (!ok) {  // let every copy this thread issued land before the CTA exits
         for (int s = 0; s < 4; ++s)

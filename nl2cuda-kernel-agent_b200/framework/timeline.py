@@ -52,11 +52,42 @@ def format_timeline(buf, counts, names=ROLES, max_events=120):
     return lines
 
 
+def format_spans(sp, ctas):
+    """Summary lines of the per-CTA records of the last traced run (g_cta_span in
+    rbf_bwd_tc.cu), in microseconds since the earliest CTA start: start (after set-up), release
+    by the previous kernel, last strip issued, end; and the tiles each CTA ran."""
+    import numpy as np
+    m48 = (1 << 48) - 1
+    sp = sp[:ctas].astype(np.int64)
+    start, end, rel = sp[:, 0] & m48, sp[:, 1] & m48, sp[:, 2] & m48
+    last, tiles = sp[:, 3] & m48, sp[:, 3] >> 48
+    t0 = start.min()
+
+    def q(name, v):
+        v = (v - t0) / 1000.0
+        return (f"{name:<11} min {v.min():7.2f}  p50 {np.median(v):7.2f}  "
+                f"p90 {np.percentile(v, 90):7.2f}  max {v.max():7.2f}")
+    lines = [q("start", start), q("released", rel), q("last strip", last), q("end", end)]
+    dur = (end - rel) / 1000.0
+    tail = (end - last) / 1000.0
+    lines.append(f"release->end  min {dur.min():7.2f}  p50 {np.median(dur):7.2f}  max {dur.max():7.2f}")
+    lines.append(f"last strip->end  p50 {np.median(tail):.2f}  max {tail.max():.2f}")
+    vals, counts = np.unique(tiles, return_counts=True)
+    lines.append("tiles per CTA: " + ", ".join(f"{int(v)} x{int(c)}" for v, c in zip(vals, counts)))
+    for v in vals:
+        sel = tiles == v
+        lines.append(f"  {int(v)} tiles: end p50 {np.median((end[sel] - t0) / 1000.0):.2f}  "
+                     f"release->end p50 {np.median(dur[sel]):.2f}")
+    return lines
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--case", choices=("rbf", "cosine_sim"), default="rbf")
     ap.add_argument("--n", type=int, default=4096, help="N = M (D = 64)")
     ap.add_argument("--dyn-pct", default="0", help="RBF_BWD_DYN_PCT for the traced runs")
+    ap.add_argument("--spans", action="store_true",
+                    help="also summarise every CTA's start, release, last strip issue and end")
     args = ap.parse_args(argv)
     import numpy as np
     import torch
@@ -83,6 +114,11 @@ def main(argv=None):
         L.rbf_debug_trace(buf.ctypes.data_as(ctypes.c_void_p), n.ctypes.data_as(ctypes.c_void_p))
     print(f"CTA 0 timeline, {args.case} backward, N = M = {N}, D = {D} (microseconds)")
     print("\n".join(format_timeline(buf, n)))
+    if args.spans:
+        sp = np.zeros((1024, 4), np.uint64)
+        L.rbf_debug_spans(sp.ctypes.data_as(ctypes.c_void_p))
+        sms = torch.cuda.get_device_properties(0).multi_processor_count
+        print("\n".join(format_spans(sp, min(sms, N // 128 * (M // 128)))))
     return 0
 
 
