@@ -199,3 +199,24 @@ def test_forward_backward_entry_refuses_the_forward_workspace(cuda_device):
     torch.cuda.synchronize()
     assert st == 3  # RBF_ERR_WORKSPACE
     assert bool((K == 7.0).all())  # refused before the forward ran
+
+
+def test_underflowing_kernel_values_vs_oracle(cuda_device):
+    """gamma * ||x - y||^2 from about 1 to 250: K runs from 0.3 through the subnormal range
+    (below 1.2e-38, 5 % of the entries) down to 0.  The exp path flushes results below 2^-126 to
+    zero; that and the matching dX / dY terms stay inside the 1e-3 gate."""
+    r = np.random.default_rng(17)
+    N, M, D = 256, 300, 64
+    X = r.standard_normal((N, D)).astype(np.float32)
+    Y = np.concatenate([X[:100] + 0.3 * r.standard_normal((100, D)),
+                        2.0 * r.standard_normal((200, D)) + 1.0]).astype(np.float32)
+    gamma = 0.35
+    G = r.standard_normal((N, M)).astype(np.float32)
+    K, dX, dY = run_path(X, Y, G, gamma)
+    Kr = oracle.forward(X, Y, gamma)
+    assert ((Kr > 1e-45) & (Kr < 1.2e-38)).mean() > 0.02 and (Kr > 1e-6).any()
+    assert_gate("K", K, Kr)
+    dXr, dYr = oracle.backward(X, Y, G, gamma)
+    assert_gate("dX", dX, dXr)
+    assert_gate("dY", dY, dYr)
+    assert np.isfinite(K).all() and (K >= 0).all()
