@@ -413,9 +413,16 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(dev)
+    # N > 1: after each rank's L2 flush, a 4-byte all-reduce lines the ranks up again before the
+    # start event.  The flush's read pass takes a different time on each GPU; without this, a
+    # rank that finished its flush early would count its wait for the others inside the step's
+    # dY reduction (measured at 2 GPUs: 124-183 us per step instead of 106-112 us).
+    align = torch.zeros(1, dtype=torch.float32, device=dev) if world > 1 else None
     evs = []
     for _ in range(args.steps):
         flush_l2()
+        if align is not None:
+            dist.all_reduce(align)
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
