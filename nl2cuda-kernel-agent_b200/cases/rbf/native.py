@@ -151,10 +151,11 @@ def rbf_backward(X, Y, G, K, gamma, workspace=None, entry="rbf_sm100_backward"):
     return [dX, dY]
 
 
-def rbf_forward_backward(X, Y, G, gamma):
+def rbf_forward_backward(X, Y, G, gamma, return_workspace=False):
     """[K, dX, dY] in one call (``rbf_sm100_forward_backward``): the forward of X, Y and the
     backward of sum(G * K), for a G known before the forward; the same values as
-    ``forward_with_workspace`` followed by ``rbf_backward`` with that workspace."""
+    ``forward_with_workspace`` followed by ``rbf_backward`` with that workspace.  With
+    ``return_workspace`` the workspace (its status word: ``read_status``) is appended."""
     _check_2d(("X", "Y", "G"), (X, Y, G))
     X, Y, G = _operand(X), _operand(Y), _operand(G)
     N, D = X.shape
@@ -170,7 +171,7 @@ def rbf_forward_backward(X, Y, G, gamma):
                                                _ptr(dY), N, M, D, float(gamma), _ptr(ws),
                                                ws.numel(), _stream(X.device)),
               "rbf_sm100_forward_backward")
-    return [K, dX, dY]
+    return [K, dX, dY, ws] if return_workspace else [K, dX, dY]
 
 
 # The ctypes helpers above, shared with the other case bound to this library (cosine_sim).

@@ -44,6 +44,12 @@ class NativeShardCompute:
         from cases.rbf import native
         return native.rbf_backward(X, Y, G, K, gamma, workspace=state)
 
+    def forward_backward(self, X, Y, G, gamma):
+        """Both passes in one library call (rbf_sm100_forward_backward: one split pass, which
+        also zeroes the backward's accumulation targets).  Returns (K, dX, dY, state)."""
+        from cases.rbf import native
+        return tuple(native.rbf_forward_backward(X, Y, G, gamma, return_workspace=True))
+
     def status(self, state):
         """Device status word of the step's workspace (0 ok, 7 a bounded wait ran out)."""
         from cases.rbf import native
@@ -122,8 +128,11 @@ def forward_backward_shard(X_local, Y, G_local, gamma, compute=None, group=None,
         if check_status:
             _raise_on_status(native.read_status(ws), "routed row-sharded step")
         return K_local, dX_local, dY
-    K_local, state = compute.forward(X_local, Y, gamma)
-    dX_local, dY = compute.backward(X_local, Y, G_local, K_local, gamma, state)
+    if hasattr(compute, "forward_backward"):
+        K_local, dX_local, dY, state = compute.forward_backward(X_local, Y, G_local, gamma)
+    else:
+        K_local, state = compute.forward(X_local, Y, gamma)
+        dX_local, dY = compute.backward(X_local, Y, G_local, K_local, gamma, state)
     if check_status and hasattr(compute, "status"):
         _raise_on_status(compute.status(state), "row-sharded step")
     if reduce_dy and dist.is_available() and dist.is_initialized():

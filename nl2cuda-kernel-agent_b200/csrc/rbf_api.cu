@@ -141,7 +141,7 @@ int forward_impl(const float* X, const float* Y, float* K, int64_t N, int64_t M,
 int backward_impl(const float* X, const float* Y, const float* G, const float* K, float* dX,
                   float* dY, int64_t N, int64_t M, int64_t D, float gamma, void* ws,
                   size_t ws_bytes, cudaStream_t stream, bool prepared,
-                  const DyRoute* route = nullptr) {
+                  const DyRoute* route = nullptr, bool pre_zeroed = false) {
   int st = check_shape(N, M, D, gamma);
   if (st) return st;
   if ((st = check_ptr(X, N * D, "X"))) return st;
@@ -162,7 +162,8 @@ int backward_impl(const float* X, const float* Y, const float* G, const float* K
     return set_detail(RBF_ERR_UNSUPPORTED, "routed dY needs M % 4 == 0 (tensor-core backward)");
   if (backward_tc_supported(N, M, D))
     return cuda_status(launch_backward_tc(X, Y, G, K, dX, dY, N, M, D, gamma, ws,
-                                          wait_config_from_env(), stream, route),
+                                          wait_config_from_env(), stream, route, Epi::kRbf,
+                                          pre_zeroed),
                        "backward launch");
   return cuda_status(launch_backward_simt(X, Y, G, K, dX, dY, N, M, D, gamma, stream),
                      "backward launch");
@@ -293,10 +294,26 @@ int rbf_sm100_forward_backward(const float* X, const float* Y, const float* G, f
   if ((st = check_ptr(G, N * M, "G"))) return st;
   if ((st = check_ptr(dX, N * D, "dX"))) return st;
   if ((st = check_ptr(dY, M * D, "dY"))) return st;
-  if (workspace_bytes < rbf_sm100_backward_workspace_bytes(N, M, D))
+  if (workspace == nullptr || workspace_bytes < rbf_sm100_backward_workspace_bytes(N, M, D))
     return set_detail(RBF_ERR_WORKSPACE, "forward-backward needs the backward workspace");
-  if ((st = forward_impl(X, Y, K, N, M, D, gamma, workspace, workspace_bytes, s))) return st;
-  return backward_impl(X, Y, G, K, dX, dY, N, M, D, gamma, workspace, workspace_bytes, s, true);
+  if (!backward_tc_supported(N, M, D)) {
+    if ((st = forward_impl(X, Y, K, N, M, D, gamma, workspace, workspace_bytes, s))) return st;
+    return backward_impl(X, Y, G, K, dX, dY, N, M, D, gamma, workspace, workspace_bytes, s, true);
+  }
+  // The split pass also zeroes the backward's accumulation targets (one launch fewer).
+  if ((st = check_ptr(X, N * D, "X"))) return st;
+  if ((st = check_ptr(Y, M * D, "Y"))) return st;
+  if ((st = check_ptr(K, N * M, "K"))) return st;
+  if (!aligned16(workspace)) return set_detail(RBF_ERR_MISALIGNED, "workspace is not 16-byte aligned");
+  if ((st = check_device())) return st;
+  const WaitConfig wc = wait_config_from_env();
+  const ZeroSpec zero = backward_zero_spec(N, M, D, workspace, dX, dY, wc);
+  if ((st = cuda_status(launch_prep(X, Y, N, M, D, workspace, s, nullptr, &zero), "split pass launch")))
+    return st;
+  if ((st = cuda_status(launch_forward_tc(X, Y, K, N, M, D, gamma, workspace, wc, s), "forward launch")))
+    return st;
+  return backward_impl(X, Y, G, K, dX, dY, N, M, D, gamma, workspace, workspace_bytes, s, true,
+                       nullptr, true);
 }
 
 int rbf_sm100_backward_shard(const float* X_local, const float* Y, const float* G_local,

@@ -1036,6 +1036,28 @@ size_t backward_scratch_bytes(int64_t N, int64_t M, int64_t D) {
   return (size_t)(rowsum_bytes(N) + kAlign);
 }
 
+ZeroSpec backward_zero_spec(int64_t N, int64_t M, int64_t D, void* ws, float* dX, float* dY,
+                            const WaitConfig& wc) {
+  ZeroSpec z;
+  const PrepLayout L = prep_layout(N, M, D);
+  const bool work = N > 0 && M > 0 && D > 0;
+  const bool tma_flush = kStageDx && (D % 4) == 0;
+  float* rowsum = ws_at<float>(ws, L.end);
+  float* counter = ws_at<float>(ws, L.end + rowsum_bytes(N));
+  if (wc.deterministic && work) {  // every partial is stored, not added: only the counter
+    z.p[0] = counter;
+    z.n[0] = 1;
+    return z;
+  }
+  z.p[0] = dX;
+  z.n[0] = N * D;
+  z.p[1] = dY;
+  z.n[1] = M * D;
+  z.p[2] = (work && tma_flush) ? rowsum : counter;  // rowsum and the counter are adjacent
+  z.n[2] = (work && tma_flush) ? rowsum_bytes(N) / 4 + 1 : (work ? 1 : 0);
+  return z;
+}
+
 bool backward_tc_supported(int64_t N, int64_t M, int64_t D) {
   (void)N; (void)D;
   return (M % 4) == 0;  // G and K rows must be 16-byte pitched for TMA
@@ -1044,7 +1066,7 @@ bool backward_tc_supported(int64_t N, int64_t M, int64_t D) {
 cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, const float* K,
                                float* dX, float* dY, int64_t N, int64_t M, int64_t D,
                                float gamma, void* ws, const WaitConfig& wc, cudaStream_t stream,
-                               const DyRoute* route, Epi epi) {
+                               const DyRoute* route, Epi epi, bool pre_zeroed) {
   cudaError_t e;
   const bool dot = epi == Epi::kDot;
   const bool routed = route != nullptr && route->world > 0;
@@ -1057,7 +1079,9 @@ cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, c
   // nothing is accumulated in place, so only the tile counter is zeroed.
   const bool det = wc.deterministic && !routed && work;
   const DetLayout DL = det ? det_layout(N, M, D) : DetLayout{};
-  if (det) {
+  if (pre_zeroed) {
+    // backward_zero_spec's ranges were zeroed by the split pass of this forward + backward.
+  } else if (det) {
     if ((e = launch_kernel(rbf_bwd_zero_kernel, dim3(1), dim3(256), 0, stream, dX, (int64_t)0,
                            dY, (int64_t)0, reinterpret_cast<float*>(counter), (int64_t)1,
                            (const int*)nullptr)) != cudaSuccess)

@@ -94,8 +94,16 @@ cudaError_t launch_forward_tc(const float* X, const float* Y, float* K, int64_t 
 
 // rbf_prep.cu: norms + TF32 hi/lo split of X and Y into the workspace.  normalize_eps != NULL:
 // the rows are first divided by (||row|| + *normalize_eps) and the norms (not squared) stored.
+// Up to three fp32 ranges that a pass zeroes besides its own work (n = 0: unused).
+struct ZeroSpec {
+  float* p[3] = {nullptr, nullptr, nullptr};
+  int64_t n[3] = {0, 0, 0};
+};
+// zero != NULL: the split pass also zeroes those ranges (the backward's accumulation targets when
+// forward and backward run as one call), so the backward needs no zeroing launch of its own.
 cudaError_t launch_prep(const float* X, const float* Y, int64_t N, int64_t M, int64_t D,
-                        void* ws, cudaStream_t stream, const float* normalize_eps = nullptr);
+                        void* ws, cudaStream_t stream, const float* normalize_eps = nullptr,
+                        const ZeroSpec* zero = nullptr);
 
 // rbf_fwd_tc.cu host helpers shared by the tensor-core kernels.
 bool make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
@@ -109,10 +117,16 @@ bool backward_tc_supported(int64_t N, int64_t M, int64_t D);
 // Workspace bytes the tensor-core backward needs after the split-pass layout (rowsum vector).
 size_t backward_scratch_bytes(int64_t N, int64_t M, int64_t D);
 // Epi::kDot: K is not read (may be NULL) and gamma is ignored.
+// pre_zeroed: the ranges of backward_zero_spec were zeroed earlier in stream order (by the split
+// pass of a one-call forward + backward), so the zeroing launch is skipped.
 cudaError_t launch_backward_tc(const float* X, const float* Y, const float* G, const float* K,
                                float* dX, float* dY, int64_t N, int64_t M, int64_t D,
                                float gamma, void* ws, const WaitConfig& wc, cudaStream_t stream,
-                               const DyRoute* route = nullptr, Epi epi = Epi::kRbf);
+                               const DyRoute* route = nullptr, Epi epi = Epi::kRbf,
+                               bool pre_zeroed = false);
+// The ranges the tensor-core backward (caller's dY, no route) zeroes before it accumulates.
+ZeroSpec backward_zero_spec(int64_t N, int64_t M, int64_t D, void* ws, float* dX, float* dY,
+                            const WaitConfig& wc);
 
 // rbf_exchange.cu: completes a routed step -- barrier, owners reduce their j-blocks over every
 // rank's slot, barrier, every rank gathers dY from the owners, the step counter advances.

@@ -13,6 +13,8 @@
 // the reference's  A / (A.norm(dim=-1, keepdim=True) + eps),  reference
 // cases/cosine_sim/reference.py:17-18); hi + lo is the unit row exactly, so the backward reads
 // the saved rows back from the split.
+#include <algorithm>
+
 #include "rbf_common.cuh"
 #include "rbf_kernels.cuh"
 #include "rbf_ptx.cuh"
@@ -27,7 +29,7 @@ __global__ void __launch_bounds__(256) prep_split_kernel(
     const float* __restrict__ X, const float* __restrict__ Y, int64_t N, int64_t M, int64_t D,
     int64_t Dp, int G, float eps, float* __restrict__ xn, float* __restrict__ yn, float* __restrict__ xhi,
     float* __restrict__ xlo, float* __restrict__ yhi, float* __restrict__ ylo,
-    int* __restrict__ status) {
+    int* __restrict__ status, ZeroSpec zero) {
   ptx::griddep_wait();
   ptx::griddep_launch_dependents();
   if (blockIdx.x == 0 && threadIdx.x == 0) *status = RBF_OK;  // fresh workspace: no error yet
@@ -82,23 +84,30 @@ __global__ void __launch_bounds__(256) prep_split_kernel(
   }
   if (!NORM) s = group_sum(s);
   if (valid && l == 0) (is_x ? xn : yn)[r] = s;
+  // Ranges the caller asked to have zeroed (the backward's accumulation targets), grid-stride.
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+#pragma unroll
+  for (int z = 0; z < 3; ++z)
+    for (int64_t k = tid; k < zero.n[z]; k += stride) zero.p[z][k] = 0.f;
 }
 
 cudaError_t launch_prep(const float* X, const float* Y, int64_t N, int64_t M, int64_t D,
-                        void* ws, cudaStream_t stream, const float* normalize_eps) {
+                        void* ws, cudaStream_t stream, const float* normalize_eps,
+                        const ZeroSpec* zero) {
   const PrepLayout L = prep_layout(N, M, D);
   const int64_t rows = N + M;
-  if (rows == 0) return cudaSuccess;
+  if (rows == 0 && (zero == nullptr || zero->n[0] + zero->n[1] + zero->n[2] == 0)) return cudaSuccess;
   const int64_t q = L.Dp / 4;  // float4 steps per row (Dp is a multiple of 32)
   const int G = q <= 8 ? 8 : (q <= 16 ? 16 : 32);
   const int rows_per_block = 8 * (32 / G);
-  const int64_t blocks = ceil_div(rows, rows_per_block);
+  const int64_t blocks = std::max<int64_t>(ceil_div(rows, rows_per_block), 1);
   const cudaError_t e = launch_kernel(
       normalize_eps != nullptr ? prep_split_kernel<true> : prep_split_kernel<false>,
       dim3((unsigned)blocks), dim3(256), 0, stream, X, Y, N, M, D, L.Dp, G,
       normalize_eps != nullptr ? *normalize_eps : 0.f, ws_at<float>(ws, L.xn), ws_at<float>(ws, L.yn), ws_at<float>(ws, L.xhi),
       ws_at<float>(ws, L.xlo), ws_at<float>(ws, L.yhi), ws_at<float>(ws, L.ylo),
-      ws_at<int>(ws, L.status));
+      ws_at<int>(ws, L.status), zero != nullptr ? *zero : ZeroSpec{});
   if (e != cudaSuccess) return e;
   note_launches(1);
   return cudaGetLastError();
