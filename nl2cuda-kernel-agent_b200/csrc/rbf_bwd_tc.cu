@@ -37,8 +37,9 @@
 // only G (W = G, half the strip bytes), keeps no row / column sums and uses c = -1, so that
 // dX = G Y and dY = G^T X; the per-row normalisation terms are added by cos_finalize_kernel.
 //
-// TMEM (512 columns): [0,64) dY acc | [64,128) dX acc | [128,256) two W buffers (hi 32 + lo
-// 32) | [256,384) W^T hi (128 columns of i) | [384,512) W^T lo.
+// TMEM (512 columns): dY acc, two halves (B = [X_hi | X_lo] stacked along N) | dX acc | W
+// buffer(s) (hi 32 + lo 32) | [256,384) W^T hi (128 columns of i) | [384,512) W^T lo; the column
+// plan by DS is TmemPlan below.
 // Shared memory (DS = 64): strip ring 4 x 32 KiB, X ring 2 x 16 KiB, Y ring 2 x 16 KiB, dX
 // staging 4 x 8 KiB.  (Build option RBF_BWD_XSTAGES=4: X ring 4 x 16 KiB, no staging; measured
 // slower.)
@@ -72,7 +73,20 @@ constexpr int YSTAGES = 2;     // Y-row ring
 constexpr int THREADS = 384;
 constexpr uint32_t BOX = 32 * 32 * 4;       // 32x32 fp32, 4 KiB
 constexpr uint32_t STRIP = 128 * 32 * 4;    // one column strip of G (or K), 16 KiB
-constexpr uint32_t COL_DY = 0, COL_DX = 64, COL_W = 128, COL_WT = 256;
+// TMEM: [0, 2 DS) the dY accumulator in two halves, W.X_hi (with W_lo.X_hi) | W_hi.X_lo: the dY
+// MMAs take B = [X_hi | X_lo] stacked along N, one MMA of N = 2 DS where two of N = DS would be
+// needed | dX | the W buffers (hi 32 | lo 32 each) | [256,512) W^T hi | lo.  DS = 64: dX at
+// 128, one W buffer at 192 (the stacked accumulator takes the second); DS = 32 (not stacked):
+// dY at 0, dX at 64, two W buffers at 128.
+constexpr uint32_t COL_DY = 0, COL_WT = 256;
+// Stacked dY MMAs at DS = 64 only: at DS = 32 two N = 32 MMAs cost no more than one of N = 64,
+// and the stacked form measured 3-5% slower there.
+template <int DS> constexpr bool kStackDy = DS == 64;
+template <int DS> struct TmemPlan {
+  static constexpr uint32_t DX = DS == 64 ? 128 : 64;
+  static constexpr uint32_t W = DS == 64 ? 192 : 128;
+  static constexpr int WBUFS = DS == 64 ? 1 : 2;
+};
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t MN_SBO = 512;       // one K group (4 rows x 128 B) of the 32B-atom layout
 constexpr uint32_t MN_LAYOUT = 1;      // descriptor layout type: 128B swizzle, 32B atom
@@ -568,6 +582,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 2 || warp == 3) {
     // ================================================================ MMA issuers
     constexpr uint32_t idesc = ptx::idesc_tf32(128, DS, 0, 1);
+    constexpr uint32_t idesc2 = ptx::idesc_tf32(128, 2 * DS, 0, 1);  // B = [X_hi | X_lo]
     if (warp == 2 && lane == 0) {
       // ---- dY: once per tile, A = W^T (TMEM lanes j, K = 128 rows i), B = X rows in 4 chunks.
       int xs = 0;
@@ -603,13 +618,20 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int k = 0; k < SR / 8; ++k) {
             const uint64_t bh = ptx::smem_desc(xb + 1024 * k, BOX, MN_SBO, MN_LAYOUT);
-            const uint64_t bl = ptx::smem_desc(xb + C::X_BYTES + 1024 * k, BOX, MN_SBO, MN_LAYOUT);
 #ifdef RBF_TRACE
             if (a.ablate & 16) continue;
 #endif
-            ptx::mma_tf32_ts(tmem + COL_DY, at + 8 * k, bh, idesc, dy_first ? 0u : 1u);
-            ptx::mma_tf32_ts(tmem + COL_DY, at + 8 * k, bl, idesc, 1);
-            ptx::mma_tf32_ts(tmem + COL_DY, at + 128 + 8 * k, bh, idesc, 1);
+            if constexpr (kStackDy<DS>) {
+              // W^T_hi . [X_hi | X_lo] (N = 2 DS: the ring entry holds hi then lo at a uniform
+              // atom stride), then W^T_lo . X_hi into the first half.
+              ptx::mma_tf32_ts(tmem + COL_DY, at + 8 * k, bh, idesc2, dy_first ? 0u : 1u);
+              ptx::mma_tf32_ts(tmem + COL_DY, at + 128 + 8 * k, bh, idesc, 1);
+            } else {
+              const uint64_t bl = ptx::smem_desc(xb + C::X_BYTES + 1024 * k, BOX, MN_SBO, MN_LAYOUT);
+              ptx::mma_tf32_ts(tmem + COL_DY, at + 8 * k, bh, idesc, dy_first ? 0u : 1u);
+              ptx::mma_tf32_ts(tmem + COL_DY, at + 8 * k, bl, idesc, 1);
+              ptx::mma_tf32_ts(tmem + COL_DY, at + 128 + 8 * k, bh, idesc, 1);
+            }
             dy_first = false;
           }
           ptx::mma_commit(&xempty[xs]);
@@ -641,7 +663,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           w_ph ^= 1u << wb;
           TRACE(3, 20 + s);
           ptx::tc_fence_after();
-          const uint32_t aw = tmem + COL_W + 64 * wb;
+          const uint32_t aw = tmem + TmemPlan<DS>::W + 64 * wb;
           const uint32_t yb = ptx::smem_u32(yring + ys * 2 * C::X_BYTES);
 #pragma unroll
           for (int k = 0; k < SR / 8; ++k) {
@@ -650,13 +672,13 @@ __global__ void __launch_bounds__(THREADS, 1)
 #ifdef RBF_TRACE
             if (a.ablate & 16) continue;
 #endif
-            ptx::mma_tf32_ts(tmem + COL_DX, aw + 8 * k, bh, idesc, (s | k) != 0 ? 1u : 0u);
-            ptx::mma_tf32_ts(tmem + COL_DX, aw + 8 * k, bl, idesc, 1);
-            ptx::mma_tf32_ts(tmem + COL_DX, aw + 32 + 8 * k, bh, idesc, 1);
+            ptx::mma_tf32_ts(tmem + TmemPlan<DS>::DX, aw + 8 * k, bh, idesc, (s | k) != 0 ? 1u : 0u);
+            ptx::mma_tf32_ts(tmem + TmemPlan<DS>::DX, aw + 8 * k, bl, idesc, 1);
+            ptx::mma_tf32_ts(tmem + TmemPlan<DS>::DX, aw + 32 + 8 * k, bh, idesc, 1);
           }
           ptx::mma_commit(&w_empty[wb]);
           ptx::mma_commit(&yempty[ys]);
-          wb ^= 1;
+          if (++wb == TmemPlan<DS>::WBUFS) wb = 0;
           if (++ys == YSTAGES) { ys = 0; yph ^= 1; }
         }
         if (!ok) break;
@@ -753,6 +775,16 @@ __global__ void __launch_bounds__(THREADS, 1)
         ptx::tc_fence_after();
         uint32_t accv[64];
         tmem_load_row<DS>(tmem + lane_base + COL_DY, accv);
+#pragma unroll
+        for (int c = 0; c < (kStackDy<DS> ? DS / 32 : 0); ++c) {  // + the W_hi.X_lo half
+          uint32_t lo_part[32];
+          ptx::tmem_ld32(tmem + lane_base + COL_DY + DS + 32 * c, lo_part);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            accv[32 * c + e] = __float_as_uint(__uint_as_float(accv[32 * c + e]) +
+                                               __uint_as_float(lo_part[e]));
+        }
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(dy_empty);
@@ -791,7 +823,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       dxf_ph ^= 1;
       ptx::tc_fence_after();
       uint32_t accv[64];
-      tmem_load_row<DS>(tmem + lane_base + COL_DX, accv);
+      tmem_load_row<DS>(tmem + lane_base + TmemPlan<DS>::DX, accv);
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(dx_empty);
@@ -885,8 +917,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #ifdef RBF_TRACE
         if (!(a.ablate & 8)) {
 #endif
-        ptx::tmem_st32(tmem + lane_base + COL_W + 64 * wb, hi);
-        ptx::tmem_st32(tmem + lane_base + COL_W + 64 * wb + 32, lo);
+        ptx::tmem_st32(tmem + lane_base + TmemPlan<DS>::W + 64 * wb, hi);
+        ptx::tmem_st32(tmem + lane_base + TmemPlan<DS>::W + 64 * wb + 32, lo);
         ptx::tmem_wait_st();
 #ifdef RBF_TRACE
         }
@@ -895,7 +927,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&w_full[wb]);
         if (lane == 0 && q == 0) TRACE(5, 30 + s);
-        wb ^= 1;
+        if (++wb == TmemPlan<DS>::WBUFS) wb = 0;
         if (s == 0 && pending) {
           if (!flush_prev()) { ok = false; break; }
           pending = false;
