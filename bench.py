@@ -20,9 +20,14 @@ small, and with one NCCL all-reduce otherwise, where that measured faster (RBF_D
 nccl forces either).  After timing, every rank checks sampled rows of K and dX and columns of dY
 of one more step against the CPU oracle ("parity" in the JSON line).
 ``value`` = whole-job GFLOP/s = (6 * N_global * M * D) / (max over ranks of the device time of
-one step).  Inputs are resident in HBM when timing starts; L2 is flushed before every timed
-step, outside the events: a 256 MiB write, then a 256 MiB read of a second buffer, so that the
-flush's own dirty lines are written back before the step rather than during it.
+one step).  The step is ``shard.forward_backward_shard``: the library's one-call forward +
+backward (rbf_sm100_forward_backward) plus the dY reduction when N > 1.  Inputs are resident in
+HBM when timing starts; L2 is flushed before every timed step, outside the events: a 256 MiB
+write, then a 256 MiB read of a second buffer, so that the flush's own dirty lines are written
+back before the step rather than during it.  With N > 1 a 4-byte all-reduce after the flush
+lines the ranks up again before the start event.  Besides the step, the line carries the
+forward (``ms_fwd``), the backward (``ms_bwd``) and the one-call forward + backward
+(``ms_fused``), each replayed alone from its own CUDA graph.
 
 ``--impl reference`` times the reference's own CPU implementation of the path (its broadcast
 ``reference.py`` forward + torch autograd, restated in oracle/reference_port.py) on the host
