@@ -29,7 +29,20 @@ class OracleCompute:
         return torch.from_numpy(dX.astype(np.float32)), torch.from_numpy(dY.astype(np.float32))
 
 
-def _worker(rank, world, port, N, M, D, gamma, out_dir):
+class OneCallOracleCompute(OracleCompute):
+    """Stand-in with the one-call entry of NativeShardCompute (forward_backward): the driver must
+    use it, not the two calls."""
+
+    def forward(self, X, Y, gamma):
+        raise AssertionError("the one-call entry should have been used")
+
+    def forward_backward(self, X, Y, G, gamma):
+        K, _ = OracleCompute.forward(self, X, Y, gamma)
+        dX, dY = OracleCompute.backward(self, X, Y, G, K, gamma, None)
+        return K, dX, dY, None
+
+
+def _worker(rank, world, port, N, M, D, gamma, out_dir, one_call=False):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     for p in (os.path.join(root, "nl2cuda-kernel-agent_b200"), root):
@@ -42,7 +55,8 @@ def _worker(rank, world, port, N, M, D, gamma, out_dir):
     Y = torch.randn(M, D, generator=g)
     G = torch.randn(N, M, generator=g)
     Xl, Gl = shard.shard_inputs(X, G, world, rank)
-    K, dX, dY = shard.forward_backward_shard(Xl, Y, Gl, gamma, compute=OracleCompute())
+    compute = OneCallOracleCompute() if one_call else OracleCompute()
+    K, dX, dY = shard.forward_backward_shard(Xl, Y, Gl, gamma, compute=compute)
     a, b = shard.row_range(N, world, rank)
     np.savez(os.path.join(out_dir, f"rank{rank}.npz"), K=K.numpy(), dX=dX.numpy(), dY=dY.numpy(),
              a=a, b=b)
@@ -62,11 +76,12 @@ def test_row_range_partitions():
             assert max(sizes) - min(sizes) <= 1
 
 
-@pytest.mark.parametrize("world", [2])
-def test_two_rank_shard_matches_unsharded(tmp_path, world):
+@pytest.mark.parametrize("world,one_call", [(2, False), (2, True)])
+def test_two_rank_shard_matches_unsharded(tmp_path, world, one_call):
     N, M, D, gamma = 37, 29, 6, 0.15
-    port = 29500 + (os.getpid() % 1000)
-    mp.spawn(_worker, args=(world, port, N, M, D, gamma, str(tmp_path)), nprocs=world, join=True)
+    port = 29500 + (os.getpid() % 1000) + (7 if one_call else 0)
+    mp.spawn(_worker, args=(world, port, N, M, D, gamma, str(tmp_path), one_call), nprocs=world,
+             join=True)
     from oracle import oracle
     g = torch.Generator().manual_seed(5)
     X = torch.randn(N, D, generator=g)
